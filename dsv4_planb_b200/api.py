@@ -1,0 +1,318 @@
+"""Drop-in ``sparse_attn_sharedkv`` for B200, over the sas_b200 C ABI.
+
+Mirrors the reference entry point ``sparse_attn_sharedkv_tilelang/api.py:129-397``
+of yangqiang2018/dsv4_planB: the same keyword arguments with the same meaning,
+the same scenario dispatch (``cmp_kv`` / ``cmp_sparse_indices`` present or not,
+api.py:196-202), the same TND / BSND handling (api.py:204-240), the same
+assertions (api.py:186-191, 247-249, 362-364) and the same return value
+(``out``, or ``(out, lse)`` when ``return_softmax_lse``, api.py:388-397).
+
+Differences, all widenings of the reference contract:
+
+* any head count N1 and any ``D_qk % 8 == 0`` (the reference pins N1 = 64,
+  D = 512, api.py:279-282); ``v_head_dim`` (default ``D_qk``) selects the
+  DeepSeek-V4 split of a 576-wide K = V row into D_v = 512 value columns;
+* ``metadata`` is accepted and checked for size but not needed: the B200
+  kernels plan their own work split over 148 SMs (no scheduler call and no
+  host sync when it is omitted); ``core_num`` is accepted and ignored;
+* extra keywords ``kernel`` ("auto" | "simt" | "tc"), ``max_seqlen_q`` (skips
+  the host read of ``cu_seqlens_q``), ``out`` / ``lse_out`` (preallocated
+  outputs) and ``check_status`` (read the device status word, synchronising).
+"""
+
+from __future__ import annotations
+
+from typing import Optional, Tuple, Union
+
+import torch
+
+from . import _lib
+
+SAS_META_SIZE = 1024
+DEFAULT_CORE_NUM = 24
+
+
+def _dtype_code(t: torch.dtype) -> int:
+    if t == torch.bfloat16:
+        return _lib.SAS_DTYPE_BF16
+    if t == torch.float16:
+        return _lib.SAS_DTYPE_FP16
+    raise ValueError(f"unsupported torch dtype {t}")
+
+
+def _i32(t: torch.Tensor, device) -> torch.Tensor:
+    return t.to(device=device, dtype=torch.int32).contiguous()
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _workspace(nbytes: int, device) -> torch.Tensor:
+    # The caching allocator makes this cheap and keeps it stream-ordered.
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+def sparse_attn_sharedkv(
+    q: torch.Tensor,
+    *,
+    ori_kv: torch.Tensor,
+    cmp_kv: Optional[torch.Tensor] = None,
+    cmp_sparse_indices: Optional[torch.Tensor] = None,
+    ori_block_table: torch.Tensor,
+    cmp_block_table: Optional[torch.Tensor] = None,
+    cu_seqlens_q: Optional[torch.Tensor] = None,
+    seqused_q: Optional[torch.Tensor] = None,
+    seqused_kv: torch.Tensor,
+    sinks: torch.Tensor,
+    metadata: Optional[torch.Tensor] = None,
+    softmax_scale: float,
+    cmp_ratio: Optional[int] = None,
+    ori_mask_mode: int = 4,
+    cmp_mask_mode: int = 3,
+    ori_win_left: int = 127,
+    ori_win_right: int = 0,
+    layout_q: str = "TND",
+    layout_kv: str = "PA_ND",
+    return_softmax_lse: bool = False,
+    core_num: int = DEFAULT_CORE_NUM,
+    topk_cmp: Optional[int] = None,
+    v_head_dim: Optional[int] = None,
+    kernel: str = "auto",
+    max_seqlen_q: Optional[int] = None,
+    out: Optional[torch.Tensor] = None,
+    lse_out: Optional[torch.Tensor] = None,
+    check_status: bool = False,
+) -> Union[torch.Tensor, Tuple[torch.Tensor, torch.Tensor]]:
+    """Sink-seeded sliding-window + compressed attention over a shared K = V cache.
+
+    Scenario 1 (SWA) when ``cmp_kv`` is None, 2 (CFA) when only
+    ``cmp_sparse_indices`` is None, 3 (SCFA) otherwise.  Returns ``out`` in
+    the layout of ``q`` (last dim ``v_head_dim``), and with
+    ``return_softmax_lse`` also the fp32 natural-log LSE ``[T, N1]`` (TND) or
+    ``[B, S, N1]`` (BSND) with the sink folded in.
+    """
+    del seqused_q, core_num  # API parity (the reference kernel does not read them either)
+    assert ori_mask_mode == 4, "only ori_mask_mode=4 supported"
+    assert cmp_mask_mode == 3 or cmp_kv is None, "only cmp_mask_mode=3 supported"
+    assert ori_win_right == 0, "only ori_win_right=0 supported"
+    assert layout_kv == "PA_ND", "only layout_kv=PA_ND supported"
+    assert layout_q in ("TND", "BSND"), f"unsupported layout_q={layout_q!r}"
+    if kernel not in _lib.KERNELS:
+        raise ValueError(f"kernel must be one of {sorted(_lib.KERNELS)}")
+    if not q.is_cuda:
+        raise ValueError("q must be a CUDA tensor (sas_b200 has no CPU path)")
+    dev = q.device
+    dtype_code = _dtype_code(q.dtype)
+
+    if cmp_kv is None:
+        scenario = 1
+    elif cmp_sparse_indices is None:
+        scenario = 2
+    else:
+        scenario = 3
+
+    # ---- flat [T, ...] view and per-request query ranges (api.py:204-240)
+    if layout_q == "TND":
+        assert cu_seqlens_q is not None, "cu_seqlens_q is required for TND"
+        T, N1, D = q.shape
+        q_flat = q
+        cu = _i32(cu_seqlens_q, dev)
+        B = cu.numel() - 1
+        q_prefix = cu[:-1]
+        act_q = (cu[1:] - cu[:-1]).contiguous()
+        if max_seqlen_q is None:
+            cu_h = cu_seqlens_q.detach().to("cpu", torch.int64)
+            max_seqlen_q = int((cu_h[1:] - cu_h[:-1]).max().item()) if B > 0 else 0
+        idx_flat = _i32(cmp_sparse_indices, dev) if scenario == 3 else None
+    else:
+        B, S_max, N1, D = q.shape
+        T = B * S_max
+        q_flat = q.reshape(T, N1, D)
+        q_prefix = torch.arange(B, dtype=torch.int32, device=dev) * S_max
+        if cu_seqlens_q is not None:
+            cu = _i32(cu_seqlens_q, dev)
+            act_q = (cu[1:] - cu[:-1]).contiguous()
+        else:
+            act_q = torch.full((B,), S_max, dtype=torch.int32, device=dev)
+        max_seqlen_q = S_max if max_seqlen_q is None else max_seqlen_q
+        if scenario == 3:
+            ci = cmp_sparse_indices
+            idx_flat = _i32(ci.reshape(T, ci.shape[2], ci.shape[3]), dev)
+        else:
+            idx_flat = None
+
+    seq_kv = _i32(seqused_kv, dev)
+
+    # ---- scenario-specific sizes (api.py:244-282)
+    max_cmp_len = 0
+    if scenario == 3:
+        N2 = idx_flat.shape[1]
+        K = topk_cmp if topk_cmp is not None else idx_flat.shape[2]
+        assert K == idx_flat.shape[2], "topk_cmp does not match cmp_sparse_indices last dim"
+    elif scenario == 2:
+        N2 = cmp_kv.shape[2]
+        K = 0
+        assert cmp_ratio is not None, "cmp_ratio is required with cmp_kv"
+        max_cmp_len = int(seqused_kv.max().item()) // cmp_ratio if seqused_kv.numel() else 0
+    else:
+        N2 = ori_kv.shape[2]
+        K = 0
+    if N2 != 1:
+        raise ValueError(f"only one KV head is supported (got N2={N2})")
+    Dv = D if v_head_dim is None else int(v_head_dim)
+    if ori_kv.shape[-1] != D:
+        raise ValueError(f"ori_kv row width {ori_kv.shape[-1]} != head_dim {D}")
+    if ori_kv.dtype != q.dtype or (cmp_kv is not None and cmp_kv.dtype != q.dtype):
+        raise ValueError("q, ori_kv and cmp_kv must share one dtype")
+
+    ori_kv_d = ori_kv.to(dev).contiguous()
+    ori_bt = _i32(ori_block_table, dev)
+    if scenario >= 2:
+        cmp_kv_d = cmp_kv.to(dev).contiguous()
+        cmp_bt = _i32(cmp_block_table, dev)
+        cmp_ratio_eff = int(cmp_ratio) if cmp_ratio is not None else 4
+    else:
+        cmp_kv_d = cmp_bt = None
+        cmp_ratio_eff = int(cmp_ratio) if cmp_ratio is not None else 4
+    sinks_d = sinks.to(device=dev, dtype=torch.float32).contiguous()
+    if metadata is not None:
+        assert metadata.numel() == SAS_META_SIZE, (
+            f"metadata must have {SAS_META_SIZE} int32 entries (got {metadata.numel()})"
+        )
+        metadata = _i32(metadata.reshape(SAS_META_SIZE), dev)
+
+    args = _lib.SasFwdArgs()
+    args.batch = B
+    args.num_tokens = T
+    args.max_q_len = int(max_seqlen_q)
+    args.num_heads = N1
+    args.num_kv_heads = N2
+    args.head_dim = D
+    args.v_head_dim = Dv
+    args.ori_block_num, args.ori_block_size = ori_kv_d.shape[0], ori_kv_d.shape[1]
+    args.ori_table_len = ori_bt.shape[1]
+    if scenario >= 2:
+        args.cmp_block_num, args.cmp_block_size = cmp_kv_d.shape[0], cmp_kv_d.shape[1]
+        args.cmp_table_len = cmp_bt.shape[1]
+    args.topk = K
+    args.cmp_ratio = cmp_ratio_eff
+    args.scenario = scenario
+    args.max_cmp_len = max_cmp_len
+    args.ori_win_left = ori_win_left
+    args.ori_win_right = ori_win_right
+    args.ori_mask_mode = ori_mask_mode
+    args.cmp_mask_mode = cmp_mask_mode
+    args.dtype = dtype_code
+    args.softmax_scale = float(softmax_scale)
+    args.kernel = _lib.KERNELS[kernel]
+
+    lib = _lib.load()
+    nbytes = _lib.ctypes.c_size_t(0)
+    _lib.check(lib.sas_workspace_size(_lib.ctypes.byref(args), _lib.ctypes.byref(nbytes)), "sas_workspace_size")
+    ws = _workspace(nbytes.value, dev)
+    if out is None:
+        out_flat = torch.empty((T, N1, Dv), dtype=q.dtype, device=dev)
+    else:
+        out_flat = out.view(T, N1, Dv)
+    if lse_out is None:
+        lse_flat = torch.empty((T, N1), dtype=torch.float32, device=dev)
+    else:
+        lse_flat = lse_out.view(T, N1)
+    q_c = q_flat.contiguous()
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    rc = lib.sas_forward(
+        _lib.ctypes.byref(args),
+        _ptr(q_c),
+        _ptr(ori_kv_d),
+        _ptr(ori_bt),
+        _ptr(cmp_kv_d),
+        _ptr(cmp_bt),
+        _ptr(idx_flat),
+        _ptr(q_prefix),
+        _ptr(act_q),
+        _ptr(seq_kv),
+        _ptr(sinks_d),
+        _ptr(metadata),
+        _ptr(out_flat),
+        _ptr(lse_flat),
+        _ptr(ws),
+        ws.numel(),
+        stream,
+    )
+    _lib.check(rc, "sas_forward")
+    if check_status:
+        st = _lib.ctypes.c_uint32(0)
+        _lib.check(lib.sas_read_status(_ptr(ws), _lib.ctypes.byref(st), stream), "sas_read_status")
+        if st.value:
+            raise RuntimeError(f"sas_forward device status: {_lib.status_names(st.value)}")
+
+    if layout_q == "TND":
+        out_r, lse_r = out_flat, lse_flat
+    else:
+        out_r = out_flat.reshape(B, T // max(B, 1), N1, Dv)
+        lse_r = lse_flat.reshape(B, T // max(B, 1), N1)
+    if return_softmax_lse:
+        return out_r, lse_r
+    return out_r
+
+
+def resolve_rows(
+    *,
+    cmp_sparse_indices: Optional[torch.Tensor],
+    ori_block_table: torch.Tensor,
+    cmp_block_table: Optional[torch.Tensor],
+    cu_seqlens_q: torch.Tensor,
+    seqused_kv: torch.Tensor,
+    num_heads: int,
+    head_dim: int,
+    ori_block_num: int,
+    ori_block_size: int,
+    cmp_block_num: int = 1,
+    cmp_block_size: int = 1,
+    cmp_ratio: int = 4,
+    scenario: int = 3,
+    ori_win_left: int = 127,
+    max_cmp_len: int = 0,
+):
+    """Run only the key-resolution step (TND) and return ``(token_info [T, 8], cmp_rows [T, cap])``.
+
+    ``token_info`` columns: b, s_global, ori_left, n_win, n_cmp, valid, s, 0.
+    ``cmp_rows`` holds physical compressed rows (-1 = unmapped block).
+    """
+    dev = ori_block_table.device
+    cu = _i32(cu_seqlens_q, dev)
+    cu_h = cu_seqlens_q.detach().to("cpu", torch.int64)
+    B = cu.numel() - 1
+    T = int(cu_h[-1].item()) if B > 0 else 0
+    max_q = int((cu_h[1:] - cu_h[:-1]).max().item()) if B > 0 else 0
+    args = _lib.SasFwdArgs()
+    args.batch, args.num_tokens, args.max_q_len = B, T, max_q
+    args.num_heads, args.num_kv_heads, args.head_dim, args.v_head_dim = num_heads, 1, head_dim, min(head_dim, 512)
+    args.ori_block_num, args.ori_block_size, args.ori_table_len = ori_block_num, ori_block_size, ori_block_table.shape[1]
+    if scenario >= 2:
+        args.cmp_block_num, args.cmp_block_size = cmp_block_num, cmp_block_size
+        args.cmp_table_len = cmp_block_table.shape[1]
+    args.topk = cmp_sparse_indices.shape[-1] if scenario == 3 else 0
+    args.cmp_ratio, args.scenario, args.max_cmp_len = cmp_ratio, scenario, max_cmp_len
+    args.ori_win_left, args.ori_mask_mode, args.cmp_mask_mode = ori_win_left, 4, 3
+    args.dtype, args.softmax_scale, args.kernel = 0, 1.0, _lib.KERNELS["simt"]
+    lib = _lib.load()
+    nbytes = _lib.ctypes.c_size_t(0)
+    _lib.check(lib.sas_workspace_size(_lib.ctypes.byref(args), _lib.ctypes.byref(nbytes)), "sas_workspace_size")
+    ws = _workspace(nbytes.value, dev)
+    cap = args.topk if scenario == 3 else (max_cmp_len if scenario == 2 else 0)
+    tinfo = torch.zeros((T, 8), dtype=torch.int32, device=dev)
+    rows = torch.full((T, max(cap, 1)), -7, dtype=torch.int32, device=dev)
+    idx = _i32(cmp_sparse_indices, dev) if scenario == 3 else None
+    bt_c = _i32(cmp_block_table, dev) if scenario >= 2 else None
+    ori_bt = _i32(ori_block_table, dev)
+    seq = _i32(seqused_kv, dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    rc = lib.sas_resolve_rows(_lib.ctypes.byref(args), _ptr(ori_bt), _ptr(bt_c), _ptr(idx), _ptr(cu[:-1]),
+                              _ptr((cu[1:] - cu[:-1]).contiguous()), _ptr(seq), _ptr(tinfo), _ptr(rows), _ptr(ws),
+                              ws.numel(), stream)
+    _lib.check(rc, "sas_resolve_rows")
+    st = _lib.ctypes.c_uint32(0)
+    _lib.check(lib.sas_read_status(_ptr(ws), _lib.ctypes.byref(st), stream), "sas_read_status")
+    return tinfo, rows[:, :cap], st.value

@@ -1,0 +1,175 @@
+/*
+ * sas_b200.h -- C ABI of the B200-native sparse_attn_sharedkv operator.
+ *
+ * Drop-in boundary for the reference yangqiang2018/dsv4_planB
+ * (sparse_attn_sharedkv_tilelang/).  Every entry point is stream-ordered,
+ * takes plain device pointers and sizes, performs no host synchronisation
+ * (except sas_read_status, whose job is to read a device word back), and
+ * returns an int status (SAS_OK or an error below; sas_strerror names it).
+ * The caller owns every buffer, including the workspace.  Pointers are CUDA
+ * device pointers on the current device; `stream` is a cudaStream_t passed
+ * as void* (NULL = the legacy default stream).
+ */
+#ifndef SAS_B200_H
+#define SAS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SAS_ABI_VERSION 1
+
+/* ---- status codes ------------------------------------------------------- */
+enum {
+    SAS_OK = 0,
+    SAS_ERR_INVALID_ARG = 1,  /* a size, pointer or mode is outside the contract */
+    SAS_ERR_UNSUPPORTED = 2,  /* valid for the reference, not implemented here */
+    SAS_ERR_WORKSPACE = 3,    /* workspace missing or smaller than *_workspace_size */
+    SAS_ERR_CUDA = 4,         /* a CUDA runtime call failed (launch, attribute, ...) */
+    SAS_ERR_DEVICE = 5        /* sas_read_status found a device-side problem */
+};
+
+/* ---- device status bits (sas_read_status) ------------------------------- */
+#define SAS_STATUS_BAD_INDEX 0x1u    /* a compressed index < -1 was skipped */
+#define SAS_STATUS_BAD_BLOCK 0x2u    /* a block-table entry >= block_num, or a position past the
+                                        table: the row was read as zeros */
+#define SAS_STATUS_NO_PROGRESS 0x4u  /* metadata: the scheduler found no row with work where the
+                                        reference loops forever (metadata.py:759-763) */
+#define SAS_STATUS_WAIT_TIMEOUT 0x8u /* a bounded device-side wait gave up */
+#define SAS_STATUS_BAD_TOKEN 0x10u   /* q_prefix[b] + s fell outside [0, num_tokens) */
+
+typedef enum { SAS_DTYPE_BF16 = 0, SAS_DTYPE_FP16 = 1 } SasDtype;
+
+/* Kernel choice for sas_forward (SasFwdArgs.kernel). */
+typedef enum { SAS_KERNEL_AUTO = 0, SAS_KERNEL_SIMT = 1, SAS_KERNEL_TC = 2 } SasKernel;
+
+/*
+ * Shape and mode of one sas_forward call.  Mirrors the compile-time
+ * parameters of the reference kernel builder
+ * (kernel.py:62-85 build_sparse_attn_sharedkv, keyed in api.py:81-101).
+ */
+typedef struct SasFwdArgs {
+    int32_t batch;          /* B: entries of q_prefix/act_q_len/act_kv_len, rows of both tables */
+    int32_t num_tokens;     /* T: rows of q, out, lse and cmp_indices */
+    int32_t max_q_len;      /* max over requests of act_q_len (the reference's max_seq) */
+    int32_t num_heads;      /* N1 query heads */
+    int32_t num_kv_heads;   /* N2; must be 1 (api.py:279-282) */
+    int32_t head_dim;       /* D_qk: row width of q and of both KV pools */
+    int32_t v_head_dim;     /* D_v <= D_qk: V is the first D_v columns of the K=V row */
+    int32_t ori_block_num, ori_block_size, ori_table_len;
+    int32_t cmp_block_num, cmp_block_size, cmp_table_len;
+    int32_t topk;           /* K: last dim of cmp_indices (scenario 3) */
+    int32_t cmp_ratio;      /* compression ratio (scenarios 2, 3) */
+    int32_t scenario;       /* 1 SWA, 2 CFA, 3 SCFA (api.py:196-202) */
+    int32_t max_cmp_len;    /* scenario 2: >= max over requests of floor(act_kv / cmp_ratio) */
+    int32_t ori_win_left;   /* sliding window: keys [s_g - ori_win_left, s_g] */
+    int32_t ori_win_right;  /* must be 0 */
+    int32_t ori_mask_mode;  /* must be 4 (band) */
+    int32_t cmp_mask_mode;  /* must be 3 */
+    int32_t dtype;          /* SasDtype of q, both pools and out */
+    float softmax_scale;
+    int32_t kernel;         /* SasKernel */
+    int32_t reserved[6];    /* must be 0 */
+} SasFwdArgs;
+
+/* Bytes of workspace sas_forward needs for `args` (256-byte aligned base). */
+int sas_workspace_size(const SasFwdArgs *args, size_t *bytes);
+
+/*
+ * The fused attention.  Replaces the JIT kernel the reference API launches
+ * (api.py:372-384; inputs kernel.py:209-237): the same eleven inputs in the
+ * same order, then the two outputs, then the workspace and stream.
+ *   q            [T, N1, D_qk]                      dtype
+ *   ori_kv       [ori_block_num, ori_block_size, 1, D_qk]
+ *   ori_block_table [B, ori_table_len] int32 (-1 = unmapped)
+ *   cmp_kv       [cmp_block_num, cmp_block_size, 1, D_qk]   (scenarios 2, 3; else NULL)
+ *   cmp_block_table [B, cmp_table_len] int32                (scenarios 2, 3; else NULL)
+ *   cmp_indices  [T, 1, K] int32, -1 padded                  (scenario 3; else NULL)
+ *   q_prefix     [B] int32: flat row of request b's first query token
+ *   act_q_len    [B] int32
+ *   act_kv_len   [B] int32 (seqused_kv)
+ *   sinks        [N1] fp32
+ *   metadata     int32[1024] from sas_metadata / the reference scheduler, or
+ *                NULL.  Accepted for interface parity; the B200 kernels plan
+ *                their own split over 148 SMs, so it is not read.
+ *   out          [T, N1, D_v] dtype; rows of no (b, s < act_q_len[b]) are zeroed
+ *   lse          [T, N1] fp32 natural-log LSE (sink folded in), or NULL
+ */
+int sas_forward(const SasFwdArgs *args, const void *q, const void *ori_kv, const int32_t *ori_block_table,
+                const void *cmp_kv, const int32_t *cmp_block_table, const int32_t *cmp_indices,
+                const int32_t *q_prefix, const int32_t *act_q_len, const int32_t *act_kv_len,
+                const float *sinks, const int32_t *metadata, void *out, float *lse, void *workspace,
+                size_t workspace_bytes, void *stream);
+
+/*
+ * Index-handling export: runs only the key-resolution step of sas_forward and
+ * copies, per flat token row, {b, s_global, ori_left, n_win, n_cmp, valid}
+ * into token_info[T][8] (int32) and the physical compressed rows
+ * (block * block_size + offset, or -1 for an unmapped block) into
+ * cmp_rows[T][row_cap], row_cap = K (scenario 3) or max_cmp_len (scenario 2).
+ * Same arguments as sas_forward minus the outputs.  No counterpart in the
+ * reference API: it exposes what golden.py:28-66 computes, for parity tests.
+ */
+int sas_resolve_rows(const SasFwdArgs *args, const int32_t *ori_block_table, const int32_t *cmp_block_table,
+                     const int32_t *cmp_indices, const int32_t *q_prefix, const int32_t *act_q_len,
+                     const int32_t *act_kv_len, int32_t *token_info, int32_t *cmp_rows, void *workspace,
+                     size_t workspace_bytes, void *stream);
+
+/*
+ * Reads the device status word a previous call on `workspace` left behind
+ * (SAS_STATUS_* bits, 0 = clean).  Synchronises `stream`.
+ */
+int sas_read_status(const void *workspace, uint32_t *status, void *stream);
+
+/* ---- metadata scheduler ----------------------------------------------------
+ * Replaces sparse_attn_sharedkv_metadata (metadata.py:1018-1086, the Python
+ * port of the aicpu SparseAttnSharedkvMetadata op) with a CUDA kernel whose
+ * int32[1024] output is bit-identical to it.
+ */
+typedef enum { SAS_LAYOUT_BSND = 0, SAS_LAYOUT_BSH = 1, SAS_LAYOUT_TND = 2, SAS_LAYOUT_OTHER = 3 } SasLayoutQ;
+typedef enum { SAS_LAYOUT_PA_ND = 0, SAS_LAYOUT_KV_TND = 1 } SasLayoutKv;
+
+typedef struct SasMetaArgs {
+    int32_t num_heads_q, num_heads_kv, head_dim;
+    int32_t n_cu_seqlens_q;      /* entries of cu_seqlens_q (0 = absent) */
+    int32_t n_cu_seqlens_ori_kv; /* entries of cu_seqlens_ori_kv (0 = absent) */
+    int32_t n_seqused_q;         /* entries of seqused_q (0 = absent) */
+    int32_t n_seqused_kv;        /* entries of seqused_kv (0 = absent) */
+    int32_t batch_size, max_seqlen_q, max_seqlen_kv;
+    int32_t ori_topk, cmp_topk, cmp_ratio;
+    int32_t ori_mask_mode, cmp_mask_mode, ori_win_left, ori_win_right;
+    int32_t layout_q;            /* SasLayoutQ */
+    int32_t layout_kv;           /* SasLayoutKv */
+    int32_t has_ori_kv, has_cmp_kv;
+    int32_t aic_core_num, aiv_core_num;
+    int32_t reserved[5];
+} SasMetaArgs;
+
+int sas_metadata_workspace_size(const SasMetaArgs *args, size_t *bytes);
+
+/* metadata_out: device int32[1024]. */
+int sas_metadata(const SasMetaArgs *args, const int32_t *cu_seqlens_q, const int32_t *cu_seqlens_ori_kv,
+                 const int32_t *seqused_q, const int32_t *seqused_kv, int32_t *metadata_out, void *workspace,
+                 size_t workspace_bytes, void *stream);
+
+/*
+ * Measurement aid: when both are non-NULL, sas_forward calls made afterwards
+ * by this host thread record `start_event` / `stop_event` (cudaEvent_t) on
+ * their stream immediately before and after the attention kernel itself, so
+ * a caller can time that kernel alone.  NULL, NULL switches it off.  Results
+ * are unaffected.  No counterpart in the reference.
+ */
+int sas_set_kernel_events(void *start_event, void *stop_event);
+
+/* ---- misc ---------------------------------------------------------------- */
+const char *sas_strerror(int status);
+int sas_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SAS_B200_H */

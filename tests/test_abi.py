@@ -1,0 +1,132 @@
+"""The C ABI library: it loads, exports what include/sas_b200.h declares, its
+structs agree with the ctypes mirror, and its argument checks reject
+out-of-contract calls before touching the device.  No GPU needed."""
+
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from dsv4_planb_b200 import _lib, build
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(REPO, "include", "sas_b200.h")
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build.build()
+    return _lib.load()
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(sas_[a-z_]+)\s*\(", text)))
+
+
+def test_header_and_binding_agree():
+    assert declared_functions() == sorted(_lib.EXPORTS)
+
+
+def test_library_exports_every_declared_symbol(lib):
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.lib_path()], capture_output=True, text=True, check=True)
+    exported = set(line.split()[-1] for line in out.stdout.splitlines() if line.strip())
+    for name in declared_functions():
+        assert name in exported, name
+        assert getattr(lib, name) is not None
+
+
+def test_struct_layout_matches_header(tmp_path):
+    src = tmp_path / "probe.c"
+    src.write_text(
+        '#include <stdio.h>\n#include <stddef.h>\n#include "sas_b200.h"\n'
+        "int main(void){printf(\"%zu %zu %zu %zu\\n\", sizeof(SasFwdArgs), sizeof(SasMetaArgs),"
+        " offsetof(SasFwdArgs, softmax_scale), offsetof(SasMetaArgs, reserved));return 0;}\n"
+    )
+    exe = tmp_path / "probe"
+    subprocess.run(["gcc", "-I", os.path.dirname(HEADER), str(src), "-o", str(exe)], check=True)
+    vals = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    assert vals == [ctypes.sizeof(_lib.SasFwdArgs), ctypes.sizeof(_lib.SasMetaArgs),
+                    _lib.SasFwdArgs.softmax_scale.offset, _lib.SasMetaArgs.reserved.offset]
+
+
+def good_args():
+    a = _lib.SasFwdArgs()
+    a.batch, a.num_tokens, a.max_q_len = 2, 2, 1
+    a.num_heads, a.num_kv_heads, a.head_dim, a.v_head_dim = 128, 1, 576, 512
+    a.ori_block_num, a.ori_block_size, a.ori_table_len = 64, 128, 32
+    a.cmp_block_num, a.cmp_block_size, a.cmp_table_len = 16, 128, 8
+    a.topk, a.cmp_ratio, a.scenario = 2048, 4, 3
+    a.ori_win_left, a.ori_win_right, a.ori_mask_mode, a.cmp_mask_mode = 127, 0, 4, 3
+    a.dtype, a.softmax_scale = _lib.SAS_DTYPE_BF16, 576 ** -0.5
+    return a
+
+
+def ws_size(lib, a):
+    n = ctypes.c_size_t(0)
+    rc = lib.sas_workspace_size(ctypes.byref(a), ctypes.byref(n))
+    return rc, n.value
+
+
+def test_workspace_size_and_validation(lib):
+    a = good_args()
+    rc, n = ws_size(lib, a)
+    assert rc == _lib.SAS_OK and n >= 2 * 8 * 4 + 2 * 2048 * 4
+    bad = [
+        ("num_kv_heads", 2, _lib.SAS_ERR_UNSUPPORTED),
+        ("ori_mask_mode", 3, _lib.SAS_ERR_UNSUPPORTED),
+        ("ori_win_right", 1, _lib.SAS_ERR_UNSUPPORTED),
+        ("cmp_mask_mode", 1, _lib.SAS_ERR_UNSUPPORTED),
+        ("scenario", 4, _lib.SAS_ERR_INVALID_ARG),
+        ("head_dim", 570, _lib.SAS_ERR_UNSUPPORTED),
+        ("v_head_dim", 600, _lib.SAS_ERR_UNSUPPORTED),
+        ("dtype", 7, _lib.SAS_ERR_INVALID_ARG),
+        ("cmp_ratio", 0, _lib.SAS_ERR_INVALID_ARG),
+        ("batch", -1, _lib.SAS_ERR_INVALID_ARG),
+        ("kernel", 9, _lib.SAS_ERR_INVALID_ARG),
+        ("ori_win_left", -1, _lib.SAS_ERR_INVALID_ARG),
+    ]
+    for field, value, want in bad:
+        b = good_args()
+        setattr(b, field, value)
+        assert ws_size(lib, b)[0] == want, field
+    b = good_args()
+    b.reserved[2] = 1
+    assert ws_size(lib, b)[0] == _lib.SAS_ERR_INVALID_ARG
+
+
+def test_forward_rejects_before_touching_the_device(lib):
+    a = good_args()
+    null = None
+    # missing workspace
+    rc = lib.sas_forward(ctypes.byref(a), 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, null, 1, 1, null, 0, null)
+    assert rc == _lib.SAS_ERR_WORKSPACE
+    # missing indices in scenario 3
+    rc = lib.sas_forward(ctypes.byref(a), 1, 1, 1, 1, 1, null, 1, 1, 1, 1, null, 1, 1, 1, 1 << 30, null)
+    assert rc == _lib.SAS_ERR_INVALID_ARG
+    # missing cmp pool in scenario 2
+    a.scenario, a.max_cmp_len = 2, 100
+    rc = lib.sas_forward(ctypes.byref(a), 1, 1, 1, null, 1, null, 1, 1, 1, 1, null, 1, 1, 1, 1 << 30, null)
+    assert rc == _lib.SAS_ERR_INVALID_ARG
+    assert lib.sas_forward(None, *([None] * 13), None, 0, None) == _lib.SAS_ERR_INVALID_ARG
+
+
+def test_metadata_validation(lib):
+    m = _lib.SasMetaArgs()
+    m.num_heads_q, m.num_heads_kv, m.head_dim = 64, 1, 512
+    m.batch_size, m.aic_core_num, m.aiv_core_num = 1, 24, 48
+    n = ctypes.c_size_t(0)
+    assert lib.sas_metadata_workspace_size(ctypes.byref(m), ctypes.byref(n)) == _lib.SAS_OK and n.value > 0
+    m.num_heads_kv = 0
+    assert lib.sas_metadata_workspace_size(ctypes.byref(m), ctypes.byref(n)) == _lib.SAS_ERR_INVALID_ARG
+    m.num_heads_kv = 128
+    assert lib.sas_metadata_workspace_size(ctypes.byref(m), ctypes.byref(n)) == _lib.SAS_ERR_INVALID_ARG
+
+
+def test_strerror_and_version(lib):
+    assert lib.sas_abi_version() == 1
+    for rc in range(6):
+        assert _lib.strerror(rc)

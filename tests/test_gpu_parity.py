@@ -1,0 +1,235 @@
+"""Parity of the CUDA sparse_attn_sharedkv against the oracle and the reference goldens.
+
+Bars: index handling bit-exact; bf16 out within
+atol 2e-2 / rtol 1e-2 of the fp32 golden; LSE within 1e-3.  The reference's
+own acceptance (_check_result / _check_lse against its bf16 golden) is checked
+too.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import golden_np as O
+from oracle.gen import PARAMSETS, ref_build_case
+from tests import _fixtures as F
+
+pytestmark = pytest.mark.gpu
+
+OUT_ATOL, OUT_RTOL = 2e-2, 1e-2
+LSE_ATOL = 1e-3
+KERNELS = ["simt", "tc"]
+
+
+@pytest.fixture(scope="module")
+def api(cuda_device):
+    from dsv4_planb_b200 import api as A
+
+    return A
+
+
+def tc_available():
+    from dsv4_planb_b200 import _lib
+
+    a = _lib.SasFwdArgs()
+    a.batch, a.num_tokens, a.max_q_len = 1, 1, 1
+    a.num_heads, a.num_kv_heads, a.head_dim, a.v_head_dim = 128, 1, 576, 512
+    a.ori_block_num, a.ori_block_size, a.ori_table_len = 1, 128, 1
+    a.cmp_block_num, a.cmp_block_size, a.cmp_table_len = 1, 128, 1
+    a.topk, a.cmp_ratio, a.scenario = 64, 4, 3
+    a.ori_win_left, a.ori_mask_mode, a.cmp_mask_mode = 127, 4, 3
+    a.dtype, a.softmax_scale, a.kernel = 0, 1.0, 2
+    n = _lib.ctypes.c_size_t()
+    return _lib.load().sas_workspace_size(_lib.ctypes.byref(a), _lib.ctypes.byref(n)) == 0
+
+
+def run(api, wl, kernel, dev, **extra):
+    kw = wl.api_kwargs()
+    for k, v in list(kw.items()):
+        if isinstance(v, torch.Tensor):
+            kw[k] = v.to(dev)
+    kw.update(extra)
+    out, lse = api.sparse_attn_sharedkv(wl.q.to(dev), return_softmax_lse=True, kernel=kernel, check_status=True, **kw)
+    torch.cuda.synchronize()
+    return out.float().cpu().numpy(), lse.cpu().numpy()
+
+
+def assert_close_to_golden(out, lse, exp_out, exp_lse, what):
+    err = np.abs(out - exp_out) - (OUT_ATOL + OUT_RTOL * np.abs(exp_out))
+    assert err.max() <= 0, f"{what}: out beyond atol/rtol by {err.max():.3e}"
+    lerr = np.abs(lse - exp_lse).max()
+    assert lerr <= LSE_ATOL, f"{what}: lse max err {lerr:.3e}"
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+@pytest.mark.parametrize("fixture_name", F.baseline_names())
+def test_baselines_match_reference_golden(api, cuda_device, kernel, fixture_name):
+    if kernel == "tc" and not tc_available():
+        pytest.skip("tensor-core path not built for these shapes")
+    case = F.load_case(fixture_name)
+    wl = F.rebuild_baseline(case)
+    if kernel == "tc" and wl.q.shape[2] % 64:
+        pytest.skip("tensor-core path needs D_qk % 64 == 0")
+    out, lse = run(api, wl, kernel, cuda_device)
+    toks = case["tokens"]
+    assert_close_to_golden(out[toks], lse[toks], case["out_fp32"], case["lse_fp32"], fixture_name)
+    # every token, against the numpy oracle (fp32 golden restatement)
+    ref_out, ref_lse, _ = O.sparse_attn_sharedkv_oracle(
+        wl.q, ori_kv=wl.ori_kv, ori_block_table=wl.ori_block_table, seqused_kv=wl.seqused_kv,
+        q_prefix=wl.cu_seqlens_q[:-1], act_q=wl.cu_seqlens_q[1:] - wl.cu_seqlens_q[:-1], sinks=wl.sinks,
+        softmax_scale=wl.softmax_scale, cmp_kv=wl.cmp_kv, cmp_block_table=wl.cmp_block_table,
+        cmp_sparse_indices=wl.cmp_sparse_indices, cmp_ratio=wl.cmp_ratio, v_head_dim=wl.v_head_dim)
+    assert_close_to_golden(out, lse, ref_out, ref_lse, fixture_name + " (oracle)")
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+@pytest.mark.parametrize("fixture_name", F.paramset_names())
+def test_reference_paramsets(api, cuda_device, kernel, fixture_name):
+    if kernel == "tc" and not tc_available():
+        pytest.skip("tensor-core path not built for these shapes")
+    name = fixture_name[len("paramset_"):-5]
+    tag = fixture_name[-4:]
+    cfg = PARAMSETS[name]
+    dtype = torch.bfloat16 if tag == "bf16" else torch.float16
+    case = F.load_case(fixture_name)
+    inp = ref_build_case(cfg, dtype)
+    dev = cuda_device
+    kw = dict(ori_kv=inp["ori_kv"].to(dev), cmp_kv=None if inp["cmp_kv"] is None else inp["cmp_kv"].to(dev),
+              cmp_sparse_indices=None if inp["cmp_sparse_indices"] is None else inp["cmp_sparse_indices"].to(dev),
+              ori_block_table=inp["ori_block_table"].to(dev),
+              cmp_block_table=None if inp["cmp_block_table"] is None else inp["cmp_block_table"].to(dev),
+              cu_seqlens_q=inp["cu_seqlens_q"].to(dev), seqused_kv=inp["seqused_kv"].to(dev),
+              sinks=inp["sinks"].to(dev), softmax_scale=cfg["softmax_scale"],
+              cmp_ratio=cfg["cmp_ratio"] if cfg["scenario"] >= 2 else None, return_softmax_lse=True, kernel=kernel,
+              check_status=True)
+    out, lse = api.sparse_attn_sharedkv(inp["q"].to(dev), **kw)
+    out = out.float().cpu().numpy()
+    lse = lse.cpu().numpy()
+    toks = case["tokens"]
+    # the reference test's own acceptance, against its low-precision golden
+    ref_low = F.low_bits_to_f32(case["out_low_bits"], tag)
+    pct, max_rel = F.check_result(out[toks], ref_low, tag)
+    assert pct >= 99.5 and max_rel < 10.0, (pct, max_rel)
+    pct, max_rel = F.check_lse(lse[toks], case["lse_low"], tag)
+    assert pct >= 99.5 and max_rel < 10.0, (pct, max_rel)
+    # north-star tolerance vs the fp32 golden (|scores| reach ~1e2 here: lse bar scaled by |lse|)
+    exp_out, exp_lse = case["out_fp32"], case["lse_fp32"]
+    err = np.abs(out[toks] - exp_out) - (OUT_ATOL + OUT_RTOL * np.abs(exp_out))
+    assert err.max() <= 0, err.max()
+    assert (np.abs(lse[toks] - exp_lse) <= LSE_ATOL * np.maximum(1.0, np.abs(exp_lse))).all()
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_bsnd_layout_and_return_types(api, cuda_device, kernel):
+    if kernel == "tc" and not tc_available():
+        pytest.skip("tensor-core path not built")
+    from dsv4_planb_b200 import workloads as W
+
+    wl = W.make_workload(name="bsnd", q_lens=[3, 3], kv_lens=[700, 1500], num_heads=128, topk=256)
+    dev = cuda_device
+    out_tnd, lse_tnd = run(api, wl, kernel, dev)
+    kw = wl.api_kwargs()
+    kw = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in kw.items()}
+    kw.pop("cu_seqlens_q")
+    kw["layout_q"] = "BSND"
+    q_bsnd = wl.q.to(dev).reshape(2, 3, 128, 576)
+    kw["cmp_sparse_indices"] = kw["cmp_sparse_indices"].reshape(2, 3, 1, -1)
+    single = api.sparse_attn_sharedkv(q_bsnd, kernel=kernel, **kw)
+    assert isinstance(single, torch.Tensor) and single.shape == (2, 3, 128, 512) and single.dtype == torch.bfloat16
+    pair = api.sparse_attn_sharedkv(q_bsnd, kernel=kernel, return_softmax_lse=True, **kw)
+    assert isinstance(pair, tuple) and len(pair) == 2
+    assert pair[1].shape == (2, 3, 128) and pair[1].dtype == torch.float32
+    torch.testing.assert_close(pair[0], single)
+    np.testing.assert_array_equal(pair[0].float().cpu().numpy().reshape(6, 128, 512), out_tnd)
+    np.testing.assert_array_equal(pair[1].cpu().numpy().reshape(6, 128), lse_tnd)
+
+
+def test_index_resolution_bit_exact(api, cuda_device):
+    """The per-token resolved compressed rows equal golden.py:28-66 mapped through the block table."""
+    for name in ("baseline_edges", "baseline_mtp_small", "baseline_c1", "baseline_prefill_small"):
+        wl = F.rebuild_baseline(F.load_case(name))
+        dev = cuda_device
+        tinfo, rows, status = api.resolve_rows(
+            cmp_sparse_indices=wl.cmp_sparse_indices.to(dev), ori_block_table=wl.ori_block_table.to(dev),
+            cmp_block_table=wl.cmp_block_table.to(dev), cu_seqlens_q=wl.cu_seqlens_q.to(dev),
+            seqused_kv=wl.seqused_kv.to(dev), num_heads=wl.q.shape[1], head_dim=wl.q.shape[2],
+            ori_block_num=wl.ori_kv.shape[0], ori_block_size=wl.ori_kv.shape[1], cmp_block_num=wl.cmp_kv.shape[0],
+            cmp_block_size=wl.cmp_kv.shape[1], cmp_ratio=wl.cmp_ratio)
+        assert status == 0
+        tinfo, rows = tinfo.cpu().numpy(), rows.cpu().numpy()
+        cu = wl.cu_seqlens_q.tolist()
+        bs = wl.cmp_kv.shape[1]
+        bt = wl.cmp_block_table.numpy()
+        for b in range(len(cu) - 1):
+            for s in range(cu[b + 1] - cu[b]):
+                t = cu[b] + s
+                win, cpos, _ = O.resolve_token_rows(scenario=3, b=b, s=s, act_q=cu[b + 1] - cu[b],
+                                                     act_kv=wl.kv_lens[b], cmp_idx_row=wl.cmp_sparse_indices[t, 0].numpy(),
+                                                     topk=wl.topk, cmp_ratio=wl.cmp_ratio, ori_win_left=127)
+                assert tinfo[t, 5] == 1 and tinfo[t, 0] == b
+                assert tinfo[t, 3] == win.size and (win.size == 0 or tinfo[t, 2] == win[0])
+                assert tinfo[t, 4] == cpos.size
+                phys = bt[b, cpos // bs].astype(np.int64)
+                expect = np.where(phys >= 0, phys * bs + cpos % bs, -1)
+                np.testing.assert_array_equal(rows[t, : cpos.size], expect, err_msg=f"{name} token {t}")
+
+
+def test_bad_index_and_block_flags(api, cuda_device):
+    from dsv4_planb_b200 import workloads as W
+
+    wl = W.make_workload(name="bad", q_lens=[1, 1], kv_lens=[900, 900], num_heads=16, topk=64)
+    dev = cuda_device
+    wl.cmp_sparse_indices[0, 0, 3] = -5  # < -1: skipped and flagged
+    kw = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in wl.api_kwargs().items()}
+    with pytest.raises(RuntimeError, match="bad_index"):
+        api.sparse_attn_sharedkv(wl.q.to(dev), check_status=True, **kw)
+    wl2 = W.make_workload(name="bad2", q_lens=[1], kv_lens=[900], num_heads=16, topk=64)
+    wl2.ori_block_table[0, 2] = wl2.ori_kv.shape[0] + 5  # beyond block_num -> zero row + flag
+    kw = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in wl2.api_kwargs().items()}
+    with pytest.raises(RuntimeError, match="bad_block"):
+        api.sparse_attn_sharedkv(wl2.q.to(dev), check_status=True, **kw)
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_unmapped_blocks_read_as_zero_rows(api, cuda_device, kernel):
+    """-1 table entries inside the used range behave like unpack_paged_kv's zero rows."""
+    if kernel == "tc" and not tc_available():
+        pytest.skip("tensor-core path not built")
+    from dsv4_planb_b200 import workloads as W
+
+    wl = W.make_workload(name="holes", q_lens=[2, 1], kv_lens=[1000, 3000], num_heads=128, topk=128)
+    wl.ori_block_table[0, 7] = -1  # the window of request 0 (positions 871..999) crosses block 7
+    wl.cmp_block_table[1, 0] = -1
+    out, lse = run(api, wl, kernel, cuda_device)
+    ref_out, ref_lse, _ = O.sparse_attn_sharedkv_oracle(
+        wl.q, ori_kv=wl.ori_kv, ori_block_table=wl.ori_block_table, seqused_kv=wl.seqused_kv,
+        q_prefix=wl.cu_seqlens_q[:-1], act_q=wl.cu_seqlens_q[1:] - wl.cu_seqlens_q[:-1], sinks=wl.sinks,
+        softmax_scale=wl.softmax_scale, cmp_kv=wl.cmp_kv, cmp_block_table=wl.cmp_block_table,
+        cmp_sparse_indices=wl.cmp_sparse_indices, cmp_ratio=wl.cmp_ratio, v_head_dim=wl.v_head_dim)
+    assert_close_to_golden(out, lse, ref_out, ref_lse, "holes")
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_full_size_decode_sampled(api, cuda_device, kernel):
+    """C2 at full size (B=64, N1=128, K=2048): sampled tokens against the oracle,
+    plus size-independent properties (finite, LSE >= sink, rows are convex
+    combinations so |out| <= max |V|)."""
+    if kernel == "tc" and not tc_available():
+        pytest.skip("tensor-core path not built")
+    from dsv4_planb_b200 import workloads as W
+
+    wl = W.config_workload("c2", device=cuda_device)
+    out, lse = run(api, wl, kernel, cuda_device)
+    assert np.isfinite(out).all() and np.isfinite(lse).all()
+    sinks = wl.sinks.cpu().numpy()
+    assert (lse >= sinks[None, :] - 1e-5).all()
+    assert np.abs(out).max() <= float(wl.ori_kv.abs().max().float().cpu()) + 1e-2
+    sample = [0, 17, 40, 63]
+    wl_c = wl.to("cpu")
+    ref_out, ref_lse, _ = O.sparse_attn_sharedkv_oracle(
+        wl_c.q, ori_kv=wl_c.ori_kv, ori_block_table=wl_c.ori_block_table, seqused_kv=wl_c.seqused_kv,
+        q_prefix=wl_c.cu_seqlens_q[:-1], act_q=wl_c.cu_seqlens_q[1:] - wl_c.cu_seqlens_q[:-1], sinks=wl_c.sinks,
+        softmax_scale=wl_c.softmax_scale, cmp_kv=wl_c.cmp_kv, cmp_block_table=wl_c.cmp_block_table,
+        cmp_sparse_indices=wl_c.cmp_sparse_indices, cmp_ratio=wl_c.cmp_ratio, v_head_dim=wl_c.v_head_dim,
+        tokens=sample)
+    assert_close_to_golden(out[sample], lse[sample], ref_out[sample], ref_lse[sample], "c2 sampled")
