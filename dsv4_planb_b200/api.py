@@ -168,6 +168,12 @@ def sparse_attn_sharedkv(
 
     ori_kv_d = ori_kv.to(dev).contiguous()
     ori_bt = _i32(ori_block_table, dev)
+    if ori_bt.dim() != 2 or ori_bt.shape[0] < B:
+        raise ValueError(f"ori_block_table must be [B>={B}, table_len] (got {tuple(ori_bt.shape)})")
+    if cmp_block_table is not None and (cmp_block_table.dim() != 2 or cmp_block_table.shape[0] < B):
+        raise ValueError(f"cmp_block_table must be [B>={B}, table_len] (got {tuple(cmp_block_table.shape)})")
+    if idx_flat is not None and (idx_flat.dim() != 3 or idx_flat.shape[0] != T):
+        raise ValueError(f"cmp_sparse_indices must hold one row per query token (got {tuple(idx_flat.shape)})")
     if scenario >= 2:
         cmp_kv_d = cmp_kv.to(dev).contiguous()
         cmp_bt = _i32(cmp_block_table, dev)

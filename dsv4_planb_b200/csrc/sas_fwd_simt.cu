@@ -4,7 +4,9 @@
 //
 // Per token the math is the reference golden (golden.py:156-200): a sink-seeded
 // online softmax over the window keys then the compressed keys, K = V, P rounded
-// to the input dtype before the PV product, out = acc / l and lse = m + ln(l).
+// to the input dtype before the PV product and lse = m + ln(l).  The output is
+// normalised by the sum of the rounded P (the weights actually applied), which
+// keeps out a convex combination of V rows; l for the LSE sums the exact P.
 // Scores are kept in the log2 domain (q pre-scaled by softmax_scale * log2 e).
 // The tensor-core path (sas_fwd_tc.cu) is the fast path for the production
 // shapes; this kernel serves the shapes it does not take.
@@ -40,7 +42,8 @@ __global__ void __launch_bounds__(kThreads) fwd_simt_kernel(SimtArgs p) {
     float *ms = ps + kHG * kKC;                                        // [kHG]
     float *ls = ms + kHG;
     float *al = ls + kHG;
-    int64_t *rid = reinterpret_cast<int64_t *>(al + kHG + (kHG & 1)); // [kKC]
+    float *lr = al + kHG;                                              // [kHG] sum of rounded P
+    int64_t *rid = reinterpret_cast<int64_t *>(lr + kHG);              // [kKC]
     int *rsrc = reinterpret_cast<int *>(rid + kKC);                    // [kKC]: 0 ori, 1 cmp, 2 masked
 
     const int t = blockIdx.x;
@@ -75,6 +78,7 @@ __global__ void __launch_bounds__(kThreads) fwd_simt_kernel(SimtArgs p) {
     if (tid < kHG) {
         ms[tid] = (h0 + tid < p.N1) ? p.sinks[h0 + tid] * 1.4426950408889634f : 0.f;
         ls[tid] = 1.f;
+        lr[tid] = 1.f;
     }
     float o[2 * kMaxPairs];
 #pragma unroll
@@ -142,13 +146,18 @@ __global__ void __launch_bounds__(kThreads) fwd_simt_kernel(SimtArgs p) {
                 const float m_new = fmaxf(m_old, mx);
                 const float alpha = exp2f(m_old - m_new);
                 const float pv = masked ? 0.f : exp2f(s - m_new);
-                float sum = pv;
+                const float pr = sas::DT<T>::round_p(pv);
+                float sum = pv, sumr = pr;
 #pragma unroll
-                for (int off = 16; off; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-                ps[h * kKC + lane] = sas::DT<T>::round_p(pv);
+                for (int off = 16; off; off >>= 1) {
+                    sum += __shfl_xor_sync(0xffffffffu, sum, off);
+                    sumr += __shfl_xor_sync(0xffffffffu, sumr, off);
+                }
+                ps[h * kKC + lane] = pr;
                 __syncwarp();
                 if (lane == 0) {
                     ls[h] = ls[h] * alpha + sum;
+                    lr[h] = lr[h] * alpha + sumr;
                     ms[h] = m_new;
                     al[h] = alpha;
                 }
@@ -180,7 +189,7 @@ __global__ void __launch_bounds__(kThreads) fwd_simt_kernel(SimtArgs p) {
     {
         const int h = tid >> 4, sub = tid & 15;
         if (h0 + h < p.N1) {
-            const float inv = 1.f / ls[h];
+            const float inv = 1.f / lr[h];
             T *orow = out + ((int64_t)t * p.N1 + h0 + h) * p.Dv;
 #pragma unroll
             for (int k = 0; k < kMaxPairs; ++k) {
@@ -196,7 +205,7 @@ __global__ void __launch_bounds__(kThreads) fwd_simt_kernel(SimtArgs p) {
 }
 
 size_t simt_smem(int Dq) {
-    return sizeof(float) * kHG * Dq + 2 * (size_t)kKC * (Dq + 8) + sizeof(float) * (kHG * kKC + 4 * kHG) +
+    return sizeof(float) * kHG * Dq + 2 * (size_t)kKC * (Dq + 8) + sizeof(float) * (kHG * kKC + 5 * kHG) +
            sizeof(int64_t) * kKC + sizeof(int) * kKC + 64;
 }
 

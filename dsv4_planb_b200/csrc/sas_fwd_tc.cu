@@ -1,14 +1,685 @@
-// Tensor-core (tcgen05) path of the fused attention -- placeholder until the
-// sm_100a kernel lands; every shape is served by the CUDA-core path meanwhile.
+// sm_100a tensor-core path of the fused sliding-window + compressed attention.
+//
+// One query token is processed by a cluster of two CTAs on two SMs that split
+// the work by role, because one SM's tensor memory cannot hold Q, S and O at
+// once (O alone, 128 heads x 512 fp32, is all 512 TMEM columns):
+//
+//   CTA rank 0 ("score CTA")                 CTA rank 1 ("output CTA")
+//   TMEM: Q (A operand, D_qk/2 cols)         TMEM: O (128 x D_v fp32)
+//         S double buffer (2 x 64 cols)
+//   warp 0  TMA tile::gather4 of 64 K rows   warp 0  TMA tile::gather4 of 64 V rows
+//           (all D_qk columns) per tile              (first D_v columns) per tile
+//   warp 1  tcgen05.mma  S = Q K^T           warp 1  tcgen05.mma  O += P V
+//           (M=128 heads, N=64 keys)                 (M=128 heads, N=D_v/2, 2 halves)
+//   warps 4-7 softmax: thread = head         warps 4-7 rescale O rows on request;
+//           sink-seeded online softmax,              epilogue O / l -> out (bf16)
+//           P (bf16) and per-head rescale
+//           factors stored into the output
+//           CTA's shared memory (DSMEM)
+//
+// Keys of a token are its window rows (padded to a multiple of 64) followed by
+// its resolved compressed rows (sas_prep.cu); masked / unmapped rows are read
+// as zeros by pointing the gather at one row past the pool.  Scores live in the
+// log2 domain.  The running max is only raised when a tile's max exceeds it by
+// more than 8 (P <= 2^8, exact in bf16 and fp32), so O is rarely rescaled; the
+// final out = O / l and lse = (m + log2 l) ln 2 equal the reference golden
+// (golden.py:156-200) up to rounding.
+//
+// Every wait is bounded by %globaltimer; a timeout sets SAS_STATUS_WAIT_TIMEOUT,
+// raises an abort flag in both CTAs and lets every role fall through to the
+// teardown, which frees TMEM after a cluster barrier.
+
+#include <cuda.h>
+
+#include <algorithm>
+#include <type_traits>
+
 #include "sas_common.cuh"
+#include "sas_tc_ptx.cuh"
+
+namespace {
+
+using namespace sas_ptx;
+
+constexpr int kBK = 64;           // keys per tile
+constexpr int kKStages = 3;       // score CTA: K ring
+constexpr int kVStages = 2;       // output CTA: V ring
+constexpr int kPStages = 2;       // P message ring (lives in the output CTA)
+constexpr int kThreads = 256;
+constexpr int kChunkBytes = kBK * 128;  // one 64-column slab of a 64-row tile (128B-swizzled)
+constexpr int kMaxDq = 576;
+constexpr int kMaxDv = 512;
+constexpr float kTau = 8.0f;      // lazy-rescale threshold (log2 units)
+constexpr uint64_t kTimeoutNs = 4000000000ull;
+
+// P message: bf16 P [128 heads][64 keys] (SW128 K-major) + per-head floats.
+constexpr int kPBytes = 128 * kBK * 2;  // 16 KiB
+constexpr int kMsgAlpha = kPBytes;
+constexpr int kMsgL = kMsgAlpha + 512;
+constexpr int kMsgM = kMsgL + 512;
+constexpr int kMsgBytes = 18 * 1024;
+
+constexpr int kTmemCols = 512;
+constexpr int kTmemS = 384;  // S buffers at columns 384 and 448 (Q uses columns [0, D_qk/2))
+
+struct Hdr {
+    uint64_t k_full[kKStages], k_empty[kKStages], s_full[2], s_free[2], q_full, p_empty[kPStages];
+    uint64_t v_full[kVStages], v_empty[kVStages], p_full[kPStages], o_full, o_empty, rs_req, rs_done, pv_done,
+        fin_ready;
+    uint32_t tmem_base;
+    volatile int abort;
+    int rs_stage;
+    int pad;
+    float fin_l[128];
+    float fin_m[128];
+};
+static_assert(sizeof(Hdr) <= 2048, "header must fit in 2 KiB");
+
+constexpr int kDataOff = 2048;
+constexpr int kScoreSmem = kDataOff + kKStages * (kMaxDq / 64) * kChunkBytes;
+constexpr int kOutSmem = kDataOff + kVStages * (kMaxDv / 64) * kChunkBytes + kPStages * kMsgBytes;
+constexpr int kSmemBytes = (kScoreSmem > kOutSmem ? kScoreSmem : kOutSmem) + 1024;  // + alignment slack
+
+struct TcArgs {
+    const void *q;
+    const int32_t *ori_bt, *tinfo, *rows;
+    const float *sinks;
+    void *out;
+    float *lse;
+    uint32_t *status;
+    int T, N1, Dq, Dv, row_cap;
+    int ori_block_num, ori_block_size, ori_table_len;
+    int ori_rows, cmp_rows;  // rows of each pool: the out-of-range row index reads zeros
+    float scale_log2;
+};
+
+struct Item {
+    int valid, b, left, n_win, n_cmp, nwt, ntiles;
+};
+
+__device__ __forceinline__ Item load_item(const TcArgs &p, int t) {
+    const int32_t *ti = p.tinfo + (int64_t)t * sas::TI_INTS;
+    Item it;
+    it.valid = ti[sas::TI_VALID];
+    it.b = ti[sas::TI_B];
+    it.left = ti[sas::TI_LEFT];
+    it.n_win = ti[sas::TI_NWIN];
+    it.n_cmp = ti[sas::TI_NCMP];
+    it.nwt = (it.n_win + kBK - 1) / kBK;
+    it.ntiles = it.valid ? it.nwt + (it.n_cmp + kBK - 1) / kBK : 0;
+    return it;
+}
+
+struct Sync {
+    Hdr *h;
+    uint32_t *status;
+    uint32_t peer_abort;  // shared::cluster address of the peer CTA's abort flag
+};
+
+__device__ __noinline__ void raise_abort(const Sync &s, uint32_t bits) {
+    sas::set_status(s.status, bits);
+    s.h->abort = 1;
+    st_cluster_u32(s.peer_abort, 1u);
+}
+
+// Wait for the phase of parity `parity` of mbarrier `bar`; false on abort / timeout.
+__device__ __forceinline__ bool wait_bar(const Sync &s, uint32_t bar, uint32_t parity, bool cluster_scope = false) {
+    uint64_t t0 = 0;
+    for (uint32_t it = 0;; ++it) {
+        if (cluster_scope ? mbar_try_cluster(bar, parity) : mbar_try(bar, parity)) return true;
+        if ((it & 15u) == 15u) {
+            if (s.h->abort) return false;
+            const uint64_t now = globaltimer();
+            if (t0 == 0) t0 = now;
+            else if (now - t0 > kTimeoutNs) {
+                raise_abort(s, SAS_STATUS_WAIT_TIMEOUT);
+                return false;
+            }
+        }
+    }
+}
+
+// Warp-uniform wait: every lane polls; if any lane gives up, all do.
+__device__ __forceinline__ bool wait_warp(const Sync &s, uint32_t bar, uint32_t parity, bool cluster_scope = false) {
+    return __all_sync(0xffffffffu, wait_bar(s, bar, parity, cluster_scope));
+}
+
+// Warp-uniform poll: true (for every lane, each having acquired the phase) once
+// any lane sees the phase complete.  A completed phase stays complete until
+// this warp arrives elsewhere, so the lanes that lagged succeed at once.
+__device__ __forceinline__ bool poll_warp(uint32_t bar, uint32_t parity) {
+    const bool mine = mbar_try(bar, parity);
+    if (!__any_sync(0xffffffffu, mine)) return false;
+    if (!mine)
+        while (!mbar_try(bar, parity)) {
+        }
+    return true;
+}
+
+// Physical row of key k of tile j of an item, or `oob` (reads as zeros).
+__device__ __forceinline__ int32_t key_row(const TcArgs &p, const Item &it, const int32_t *crow, int j, int k,
+                                           int oob) {
+    if (j < it.nwt) {
+        const int slot = j * kBK + k;
+        if (slot >= it.n_win) return oob;
+        const int64_t r = sas::paged_row(p.ori_bt, it.b, p.ori_table_len, p.ori_block_size, p.ori_block_num,
+                                         (int64_t)it.left + slot, p.status);
+        return r >= 0 ? (int32_t)r : oob;
+    }
+    const int c = (j - it.nwt) * kBK + k;
+    if (c >= it.n_cmp) return oob;
+    const int32_t r = crow[c];
+    return r >= 0 ? r : oob;
+}
+
+// Producer warp: gathers `nch` 64-column slabs of 64 rows per tile into a ring.
+__device__ void producer(const TcArgs &p, const Sync &sy, const CUtensorMap *ori_map, const CUtensorMap *cmp_map,
+                         uint8_t *ring, uint64_t *full, uint64_t *empty, int stages, int nch) {
+    const int lane = threadIdx.x & 31;
+    uint32_t cnt = 0;
+    const uint32_t stage_bytes = (uint32_t)nch * kChunkBytes;
+    for (int t = cluster_id_x(); t < p.T; t += ncluster_x()) {
+        const Item it = load_item(p, t);
+        const int32_t *crow = p.rows + (int64_t)t * p.row_cap;
+        for (int j = 0; j < it.ntiles; ++j, ++cnt) {
+            const int st = cnt % stages;
+            if (!wait_warp(sy, smem_u32(&empty[st]), ((cnt / stages) & 1) ^ 1)) return;
+            const bool win = j < it.nwt;
+            const int oob = win ? p.ori_rows : p.cmp_rows;
+            const int32_t ya = key_row(p, it, crow, j, 2 * lane, oob);
+            const int32_t yb = key_row(p, it, crow, j, 2 * lane + 1, oob);
+            const int g0 = (2 * lane) & 31, g1 = (2 * lane + 1) & 31;
+            const int32_t y0 = __shfl_sync(0xffffffffu, ya, g0), y1 = __shfl_sync(0xffffffffu, yb, g0);
+            const int32_t y2 = __shfl_sync(0xffffffffu, ya, g1), y3 = __shfl_sync(0xffffffffu, yb, g1);
+            const uint32_t bar = smem_u32(&full[st]);
+            if (lane == 0) mbar_arrive_expect_tx(bar, stage_bytes);
+            __syncwarp();
+            if (lane < 16) {
+                const uint32_t dst = smem_u32(ring + (size_t)st * stage_bytes) + lane * 512;
+                const CUtensorMap *map = win ? ori_map : cmp_map;
+                for (int c = 0; c < nch; ++c) tma_gather4(dst + c * kChunkBytes, map, c * 64, y0, y1, y2, y3, bar);
+            }
+            __syncwarp();
+        }
+    }
+}
+
+template <bool kBF16>
+__global__ void __launch_bounds__(kThreads, 1)
+    fwd_tc_kernel(const TcArgs p, const __grid_constant__ CUtensorMap ori_map,
+                  const __grid_constant__ CUtensorMap cmp_map) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    Hdr *hd = reinterpret_cast<Hdr *>(smem);
+    uint8_t *data = smem + kDataOff;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const int qch = p.Dq / 64, vch = p.Dv / 64;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kKStages; ++i) {
+            mbar_init(smem_u32(&hd->k_full[i]), 1);
+            mbar_init(smem_u32(&hd->k_empty[i]), 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(smem_u32(&hd->s_full[i]), 1);
+            mbar_init(smem_u32(&hd->s_free[i]), 4);
+        }
+        mbar_init(smem_u32(&hd->q_full), 4);
+        for (int i = 0; i < kPStages; ++i) {
+            mbar_init(smem_u32(&hd->p_empty[i]), 1);
+            mbar_init(smem_u32(&hd->p_full[i]), 4);
+        }
+        for (int i = 0; i < kVStages; ++i) {
+            mbar_init(smem_u32(&hd->v_full[i]), 1);
+            mbar_init(smem_u32(&hd->v_empty[i]), 1);
+        }
+        mbar_init(smem_u32(&hd->o_full), 1);
+        mbar_init(smem_u32(&hd->o_empty), 4);
+        mbar_init(smem_u32(&hd->rs_req), 1);
+        mbar_init(smem_u32(&hd->rs_done), 4);
+        mbar_init(smem_u32(&hd->pv_done), 1);
+        mbar_init(smem_u32(&hd->fin_ready), 1);
+        hd->abort = 0;
+        hd->rs_stage = 0;
+        mbar_fence_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(&hd->tmem_base), kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // both CTAs' barriers are initialised before any remote arrive
+    tc_fence_after();
+    const uint32_t tmem = hd->tmem_base;
+    Sync sy{hd, p.status, map_to_cta(smem_u32((const void *)&hd->abort), rank ^ 1u)};
+
+    if (rank == 0) {
+        // ======================= score CTA =======================
+        uint8_t *kbuf = data;
+        const uint32_t kstage = (uint32_t)qch * kChunkBytes;
+        if (warp == 0) {
+            producer(p, sy, &ori_map, &cmp_map, kbuf, hd->k_full, hd->k_empty, kKStages, qch);
+        } else if (warp == 1) {
+            constexpr uint32_t idesc = idesc_f16(kBF16 ? 1u : 0u, 128, kBK, 0);
+            uint32_t kc = 0, sc = 0, qc = 0;
+            for (int t = cluster_id_x(); t < p.T; t += ncluster_x()) {
+                const Item it = load_item(p, t);
+                if (it.ntiles == 0) continue;
+                if (!wait_warp(sy, smem_u32(&hd->q_full), qc & 1)) goto done;
+                ++qc;
+                tc_fence_after();
+                for (int j = 0; j < it.ntiles; ++j, ++kc, ++sc) {
+                    const int ks = kc % kKStages, sb = sc & 1;
+                    if (!wait_warp(sy, smem_u32(&hd->k_full[ks]), (kc / kKStages) & 1)) goto done;
+                    if (!wait_warp(sy, smem_u32(&hd->s_free[sb]), ((sc >> 1) & 1) ^ 1)) goto done;
+                    tc_fence_after();
+                    if (lane == 0) {
+                        const uint32_t kb = smem_u32(kbuf + (size_t)ks * kstage);
+                        const uint32_t d = tmem + kTmemS + sb * kBK;
+                        for (int kk = 0; kk < p.Dq / 16; ++kk) {
+                            const uint64_t bdesc = sdesc_sw128(kb + (kk >> 2) * kChunkBytes + (kk & 3) * 32, 16, 1024);
+                            mma_ts(d, tmem + kk * 8, bdesc, idesc, kk > 0 ? 1u : 0u);
+                        }
+                        tc_commit(smem_u32(&hd->k_empty[ks]));
+                        tc_commit(smem_u32(&hd->s_full[sb]));
+                    }
+                    __syncwarp();
+                }
+            }
+        } else if (warp >= 4) {
+            const int h = threadIdx.x - 128;
+            const uint32_t lane_base = (uint32_t)((warp - 4) * 32) << 16;
+            const uint32_t msg0 = map_to_cta(smem_u32(data + kVStages * vch * kChunkBytes), 1);
+            const uint32_t pfull0 = map_to_cta(smem_u32(&hd->p_full[0]), 1);
+            const float sink2 = h < p.N1 ? p.sinks[h] * 1.4426950408889634f : 0.f;
+            uint32_t sc = 0, pc = 0;
+            for (int t = cluster_id_x(); t < p.T; t += ncluster_x()) {
+                const Item it = load_item(p, t);
+                if (it.ntiles == 0) {
+                    if (p.lse && h < p.N1) p.lse[(int64_t)t * p.N1 + h] = it.valid ? p.sinks[h] : 0.f;
+                    continue;
+                }
+                // ---- Q row h -> TMEM (A operand: 2 elements per 32-bit column)
+                {
+                    const uint4 *qrow = reinterpret_cast<const uint4 *>(
+                        reinterpret_cast<const uint16_t *>(p.q) + ((int64_t)t * p.N1 + (h < p.N1 ? h : 0)) * p.Dq);
+                    for (int c = 0; c < qch; ++c) {
+                        uint32_t r[32];
+#pragma unroll
+                        for (int v = 0; v < 8; ++v) {
+                            uint4 x = h < p.N1 ? __ldg(qrow + c * 8 + v) : make_uint4(0, 0, 0, 0);
+                            r[4 * v] = x.x;
+                            r[4 * v + 1] = x.y;
+                            r[4 * v + 2] = x.z;
+                            r[4 * v + 3] = x.w;
+                        }
+                        tmem_st32(tmem + lane_base + c * 32, r);
+                    }
+                    tc_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(smem_u32(&hd->q_full));
+                }
+                // l: sum of the unrounded P (for the LSE); lr: sum of P as rounded for the PV
+                // product, the normaliser of O (the weights of the average are then the ones used)
+                float m = sink2, l = 1.f, lr = 1.f;
+                for (int j = 0; j < it.ntiles; ++j, ++sc, ++pc) {
+                    const int sb = sc & 1;
+                    if (!wait_warp(sy, smem_u32(&hd->s_full[sb]), (sc >> 1) & 1)) goto done;
+                    tc_fence_after();
+                    uint32_t sr[64];
+                    tmem_ld32(tmem + lane_base + kTmemS + sb * kBK, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+                    tmem_ld32(tmem + lane_base + kTmemS + sb * kBK + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+                    tc_wait_ld();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(smem_u32(&hd->s_free[sb]));
+                    const int nvalid = j < it.nwt ? min(kBK, it.n_win - j * kBK) : min(kBK, it.n_cmp - (j - it.nwt) * kBK);
+                    float mx = -INFINITY;
+#pragma unroll
+                    for (int k = 0; k < kBK; ++k) {
+                        const float x = k < nvalid ? __uint_as_float(sr[k]) * p.scale_log2 : -INFINITY;
+                        sr[k] = __float_as_uint(x);
+                        mx = fmaxf(mx, x);
+                    }
+                    float alpha = 1.f;
+                    bool need = false;
+                    if (j == 0) {
+                        const float mn = fmaxf(m, mx);
+                        const float a0 = exp2f(m - mn);
+                        l *= a0;
+                        lr *= a0;
+                        m = mn;
+                    } else if (mx > m + kTau) {
+                        alpha = exp2f(m - mx);
+                        l *= alpha;
+                        lr *= alpha;
+                        m = mx;
+                        need = true;
+                    }
+                    uint32_t pk[32];
+                    float sum = 0.f, sumr = 0.f;
+#pragma unroll
+                    for (int k = 0; k < kBK; k += 2) {
+                        const float p0 = exp2f(__uint_as_float(sr[k]) - m);
+                        const float p1 = exp2f(__uint_as_float(sr[k + 1]) - m);
+                        sum += p0 + p1;
+                        float2 pr;
+                        if constexpr (kBF16) {
+                            __nv_bfloat162 v = __floats2bfloat162_rn(p0, p1);
+                            pk[k >> 1] = *reinterpret_cast<uint32_t *>(&v);
+                            pr = __bfloat1622float2(v);
+                        } else {
+                            __half2 v = __floats2half2_rn(p0, p1);
+                            pk[k >> 1] = *reinterpret_cast<uint32_t *>(&v);
+                            pr = __half22float2(v);
+                        }
+                        sumr += pr.x + pr.y;
+                    }
+                    l += sum;
+                    lr += sumr;
+                    (void)need;
+                    const bool last = j == it.ntiles - 1;
+                    const int ps = pc % kPStages;
+                    if (!wait_warp(sy, smem_u32(&hd->p_empty[ps]), ((pc / kPStages) & 1) ^ 1, true)) goto done;
+                    const uint32_t msg = msg0 + ps * kMsgBytes;
+                    const uint32_t prow = msg + (h >> 3) * 1024 + (h & 7) * 128;
+#pragma unroll
+                    for (int cc = 0; cc < 8; ++cc)
+                        st_cluster_v4(prow + ((cc ^ (h & 7)) << 4), pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2],
+                                      pk[4 * cc + 3]);
+                    st_cluster_u32(msg + kMsgAlpha + h * 4, __float_as_uint(alpha));
+                    if (last) {
+                        st_cluster_u32(msg + kMsgL + h * 4, __float_as_uint(lr));
+                        st_cluster_u32(msg + kMsgM + h * 4, __float_as_uint(m));
+                    }
+                    fence_proxy_async_all();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_remote(pfull0 + ps * 8);
+                }
+                if (p.lse && h < p.N1) p.lse[(int64_t)t * p.N1 + h] = (m + log2f(l)) * 0.6931471805599453f;
+            }
+            // every P stage must be handed back before this CTA may exit
+            for (int s2 = 0; s2 < kPStages; ++s2) {
+                if ((int)pc > s2) {
+                    const uint32_t n = (pc - s2 + kPStages - 1) / kPStages;
+                    if (!wait_warp(sy, smem_u32(&hd->p_empty[s2]), (n - 1) & 1, true)) goto done;
+                }
+            }
+        }
+    } else {
+        // ======================= output CTA =======================
+        uint8_t *vbuf = data;
+        uint8_t *msgs = data + kVStages * vch * kChunkBytes;
+        const uint32_t vstage = (uint32_t)vch * kChunkBytes;
+        if (warp == 0) {
+            producer(p, sy, &ori_map, &cmp_map, vbuf, hd->v_full, hd->v_empty, kVStages, vch);
+        } else if (warp == 1) {
+            const uint32_t nhalf = (uint32_t)p.Dv / 2;
+            const uint32_t idesc = idesc_f16(kBF16 ? 1u : 0u, 128, nhalf, 1);
+            uint32_t vc = 0, pc = 0, oc = 0, pvc = 0, rsc = 0;
+            for (int t = cluster_id_x(); t < p.T; t += ncluster_x()) {
+                const Item it = load_item(p, t);
+                if (it.ntiles == 0) continue;
+                if (!wait_warp(sy, smem_u32(&hd->o_empty), (oc & 1) ^ 1)) goto done;
+                ++oc;
+                for (int j = 0; j < it.ntiles; ++j, ++vc, ++pc) {
+                    const int ps = pc % kPStages, vs = vc % kVStages;
+                    if (!wait_warp(sy, smem_u32(&hd->p_full[ps]), (pc / kPStages) & 1, true)) goto done;
+                    if (!wait_warp(sy, smem_u32(&hd->v_full[vs]), (vc / kVStages) & 1)) goto done;
+                    uint8_t *msg = msgs + ps * kMsgBytes;
+                    bool need = false;
+                    for (int i = lane; i < 128; i += 32)
+                        need |= reinterpret_cast<const float *>(msg + kMsgAlpha)[i] != 1.f;
+                    if (__any_sync(0xffffffffu, need) && j > 0) {
+                        // rescale O: wait for every PV product so far, then let warps 4-7 scale the rows
+                        if (lane == 0) tc_commit(smem_u32(&hd->pv_done));
+                        __syncwarp();
+                        if (!wait_warp(sy, smem_u32(&hd->pv_done), pvc & 1)) goto done;
+                        ++pvc;
+                        if (lane == 0) {
+                            hd->rs_stage = ps;
+                            mbar_arrive(smem_u32(&hd->rs_req));
+                        }
+                        __syncwarp();
+                        if (!wait_warp(sy, smem_u32(&hd->rs_done), rsc & 1)) goto done;
+                        ++rsc;
+                    }
+                    const bool last = j == it.ntiles - 1;
+                    if (last) {
+                        for (int i = lane; i < 128; i += 32) {
+                            hd->fin_l[i] = reinterpret_cast<const float *>(msg + kMsgL)[i];
+                            hd->fin_m[i] = reinterpret_cast<const float *>(msg + kMsgM)[i];
+                        }
+                        __syncwarp();
+                        if (lane == 0) {
+                            __threadfence_block();
+                            mbar_arrive(smem_u32(&hd->fin_ready));
+                        }
+                    }
+                    tc_fence_after();
+                    fence_proxy_async_smem();
+                    if (lane == 0) {
+                        const uint32_t pa = smem_u32(msg);
+                        const uint32_t vb = smem_u32(vbuf + (size_t)vs * vstage);
+                        for (int hf = 0; hf < 2; ++hf) {
+                            for (int kk = 0; kk < kBK / 16; ++kk) {
+                                const uint64_t adesc = sdesc_sw128(pa + kk * 32, 16, 1024);
+                                const uint64_t bdesc =
+                                    sdesc_sw128(vb + (hf * nhalf / 64) * kChunkBytes + kk * 2048, kChunkBytes, 1024);
+                                mma_ss(tmem + hf * nhalf, adesc, bdesc, idesc, (j > 0 || kk > 0) ? 1u : 0u);
+                            }
+                        }
+                        tc_commit(smem_u32(&hd->v_empty[vs]));
+                        tc_commit_mc(smem_u32(&hd->p_empty[ps]), (uint16_t)1);
+                        if (last) tc_commit(smem_u32(&hd->o_full));
+                    }
+                    __syncwarp();
+                }
+            }
+        } else if (warp >= 4) {
+            const int h = threadIdx.x - 128;
+            const uint32_t lane_base = (uint32_t)((warp - 4) * 32) << 16;
+            uint32_t ofc = 0, rsc = 0, frc = 0;
+            typedef typename std::conditional<kBF16, __nv_bfloat16, __half>::type OT;
+            for (int t = cluster_id_x(); t < p.T; t += ncluster_x()) {
+                const Item it = load_item(p, t);
+                OT *orow = reinterpret_cast<OT *>(p.out) + ((int64_t)t * p.N1 + (h < p.N1 ? h : 0)) * p.Dv;
+                if (it.ntiles == 0) {
+                    if (h < p.N1)
+                        for (int d = 0; d < p.Dv; d += 8) *reinterpret_cast<uint4 *>(orow + d) = make_uint4(0, 0, 0, 0);
+                    continue;
+                }
+                // serve rescale requests until the item's O is complete
+                uint64_t t0 = 0;
+                for (uint32_t it2 = 0;; ++it2) {
+                    if (poll_warp(smem_u32(&hd->rs_req), rsc & 1)) {
+                        ++rsc;
+                        tc_fence_after();
+                        const float a = reinterpret_cast<const float *>(msgs + hd->rs_stage * kMsgBytes + kMsgAlpha)[h];
+                        if (__any_sync(0xffffffffu, a != 1.f)) {
+                            for (int c = 0; c < p.Dv / 32; ++c) {
+                                uint32_t r[32];
+                                tmem_ld32(tmem + lane_base + c * 32, r);
+                                tc_wait_ld();
+#pragma unroll
+                                for (int k = 0; k < 32; ++k) r[k] = __float_as_uint(__uint_as_float(r[k]) * a);
+                                tmem_st32(tmem + lane_base + c * 32, r);
+                            }
+                            tc_wait_st();
+                        }
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(smem_u32(&hd->rs_done));
+                        t0 = 0;
+                        continue;
+                    }
+                    if (poll_warp(smem_u32(&hd->o_full), ofc & 1)) break;
+                    if ((it2 & 15u) == 15u) {
+                        if (hd->abort) goto done;
+                        const uint64_t now = globaltimer();
+                        if (t0 == 0) t0 = now;
+                        else if (now - t0 > kTimeoutNs) {
+                            raise_abort(sy, SAS_STATUS_WAIT_TIMEOUT);
+                            goto done;
+                        }
+                    }
+                }
+                ++ofc;
+                if (!wait_warp(sy, smem_u32(&hd->fin_ready), frc & 1)) goto done;
+                ++frc;
+                tc_fence_after();
+                const float inv = 1.f / hd->fin_l[h];
+                for (int c = 0; c < p.Dv / 32; ++c) {
+                    uint32_t r[32];
+                    tmem_ld32(tmem + lane_base + c * 32, r);
+                    tc_wait_ld();
+                    if (h < p.N1) {
+                        uint32_t w[16];
+#pragma unroll
+                        for (int k = 0; k < 16; ++k) {
+                            const float x0 = __uint_as_float(r[2 * k]) * inv, x1 = __uint_as_float(r[2 * k + 1]) * inv;
+                            if constexpr (kBF16) {
+                                __nv_bfloat162 v = __floats2bfloat162_rn(x0, x1);
+                                w[k] = *reinterpret_cast<uint32_t *>(&v);
+                            } else {
+                                __half2 v = __floats2half2_rn(x0, x1);
+                                w[k] = *reinterpret_cast<uint32_t *>(&v);
+                            }
+                        }
+                        uint4 *dst = reinterpret_cast<uint4 *>(orow + c * 32);
+#pragma unroll
+                        for (int v = 0; v < 4; ++v) dst[v] = make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&hd->o_empty));
+            }
+        }
+    }
+done:
+    __syncwarp();
+    if (hd->abort) {
+        // let in-flight TMA / MMA work land before the shared memory goes away
+        const uint64_t t0 = globaltimer();
+        while (globaltimer() - t0 < 20000000ull) {
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// Row-gather tensor map over a paged pool viewed as [rows, D] (box: 64 columns x 1 row, 128B swizzle).
+int make_map(CUtensorMap *map, const void *base, int64_t rows, int D, bool bf16) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return SAS_ERR_CUDA;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return SAS_ERR_INVALID_ARG;
+    cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)D * 2};
+    cuuint32_t box[2] = {64, 1};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                    const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? SAS_OK : SAS_ERR_CUDA;
+}
+
+} // namespace
 
 namespace sas_host {
 
-bool tc_supported(const SasFwdArgs &) { return false; }
+bool tc_supported(const SasFwdArgs &a) {
+    return a.num_heads >= 1 && a.num_heads <= 128 && a.head_dim % 64 == 0 && a.head_dim <= kMaxDq &&
+           a.v_head_dim % 128 == 0 && a.v_head_dim <= kMaxDv && a.v_head_dim <= a.head_dim;
+}
+
 size_t tc_workspace(const SasFwdArgs &) { return 0; }
-int launch_fwd_tc(const SasFwdArgs &, const sas::FwdLayout &, char *, const void *, const void *, const int32_t *,
-                  const void *, const float *, void *, float *, cudaStream_t) {
-    return SAS_ERR_UNSUPPORTED;
+
+int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const void *q, const void *ori_kv,
+                  const int32_t *ori_bt, const void *cmp_kv, const float *sinks, void *out, float *lse,
+                  cudaStream_t s) {
+    if (a.num_tokens == 0) return SAS_OK;
+    const bool bf16 = a.dtype == SAS_DTYPE_BF16;
+    TcArgs p;
+    p.q = q;
+    p.ori_bt = ori_bt;
+    p.tinfo = reinterpret_cast<const int32_t *>(ws + L.token_info);
+    p.rows = reinterpret_cast<const int32_t *>(ws + L.cmp_rows);
+    p.sinks = sinks;
+    p.out = out;
+    p.lse = lse;
+    p.status = reinterpret_cast<uint32_t *>(ws + L.status);
+    p.T = a.num_tokens;
+    p.N1 = a.num_heads;
+    p.Dq = a.head_dim;
+    p.Dv = a.v_head_dim;
+    p.row_cap = (int)L.row_cap;
+    p.ori_block_num = a.ori_block_num;
+    p.ori_block_size = a.ori_block_size;
+    p.ori_table_len = a.ori_table_len;
+    p.ori_rows = a.ori_block_num * a.ori_block_size;
+    p.cmp_rows = a.scenario >= 2 ? a.cmp_block_num * a.cmp_block_size : p.ori_rows;
+    p.scale_log2 = a.softmax_scale * 1.4426950408889634f;
+    CUtensorMap ori_map, cmp_map;
+    int rc = make_map(&ori_map, ori_kv, p.ori_rows, a.head_dim, bf16);
+    if (rc) return rc;
+    rc = make_map(&cmp_map, a.scenario >= 2 ? cmp_kv : ori_kv, p.cmp_rows, a.head_dim, bf16);
+    if (rc) return rc;
+
+    static bool attr_done[2] = {false, false};
+    const int di = bf16 ? 0 : 1;
+    if (!attr_done[di]) {
+        cudaError_t e = bf16 ? cudaFuncSetAttribute(fwd_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                    kSmemBytes)
+                             : cudaFuncSetAttribute(fwd_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                    kSmemBytes);
+        if (check_cuda(e)) return SAS_ERR_CUDA;
+        attr_done[di] = true;
+    }
+    static int num_sms = 0;
+    if (!num_sms) {
+        int dev = 0;
+        if (check_cuda(cudaGetDevice(&dev))) return SAS_ERR_CUDA;
+        if (check_cuda(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev))) return SAS_ERR_CUDA;
+    }
+    const int clusters = std::max(1, std::min(a.num_tokens, num_sms / 2));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * clusters, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = bf16 ? cudaLaunchKernelEx(&cfg, fwd_tc_kernel<true>, p, ori_map, cmp_map)
+                         : cudaLaunchKernelEx(&cfg, fwd_tc_kernel<false>, p, ori_map, cmp_map);
+    return check_cuda(e);
 }
 
 } // namespace sas_host
