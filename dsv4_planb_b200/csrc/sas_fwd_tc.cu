@@ -7,19 +7,23 @@
 //   CTA rank 0 ("score CTA")                 CTA rank 1 ("output CTA")
 //   TMEM: Q (A operand, D_qk/2 cols)         TMEM: O (128 x D_v fp32)
 //         S double buffer (2 x 64 cols)
-//   warp 0  TMA tile::gather4 of 64 K rows   warp 0  TMA tile::gather4 of 64 V rows
-//           (all D_qk columns) per tile              (first D_v columns) per tile
-//   warp 1  tcgen05.mma  S = Q K^T           warp 1  tcgen05.mma  O += P V
+//   warps 4-7 gather 64 K rows (all D_qk     warps 4-7 gather 64 V rows (first D_v
+//           columns) per tile: 16-byte               columns) per tile
+//           cp.async into the 128B-swizzled
+//           UMMA layout
+//   warp 8  tcgen05.mma  S = Q K^T           warp 8  tcgen05.mma  O += P V
 //           (M=128 heads, N=64 keys)                 (M=128 heads, N=D_v/2, 2 halves)
-//   warps 4-7 softmax: thread = head         warps 4-7 rescale O rows on request;
-//           sink-seeded online softmax,              epilogue O / l -> out (bf16)
-//           P (bf16) and per-head rescale
-//           factors stored into the output
-//           CTA's shared memory (DSMEM)
+//   warps 0-3 softmax: thread = head         warps 0-3 rescale O rows on request;
+//           sink-seeded online softmax;              epilogue O / l -> out
+//           P (bf16) and per-head factors
+//           go to the output CTA's shared
+//           memory by st.async, which
+//           completes its mbarrier (DSMEM)
 //
 // Keys of a token are its window rows (padded to a multiple of 64) followed by
 // its resolved compressed rows (sas_prep.cu); masked / unmapped rows are read
-// as zeros by pointing the gather at one row past the pool.  Scores live in the
+// as zeros (cp.async with source size 0).  (TMA tile::gather4 was measured at
+// ~40 ns per 512-byte gather per SM here, too slow to feed the tensor cores.)  Scores live in the
 // log2 domain.  The running max is only raised when a tile's max exceeds it by
 // more than 8 (P <= 2^8, exact in bf16 and fp32), so O is rarely rescaled; the
 // final out = O / l and lse = (m + log2 l) ln 2 equal the reference golden
@@ -45,7 +49,7 @@ constexpr int kBK = 64;           // keys per tile
 constexpr int kKStages = 3;       // score CTA: K ring
 constexpr int kVStages = 2;       // output CTA: V ring
 constexpr int kPStages = 2;       // P message ring (lives in the output CTA)
-constexpr int kThreads = 256;
+constexpr int kThreads = 288;       // warps 0-3 softmax / epilogue, 4-7 gather, 8 MMA
 constexpr int kChunkBytes = kBK * 128;  // one 64-column slab of a 64-row tile (128B-swizzled)
 constexpr int kMaxDq = 576;
 constexpr int kMaxDv = 512;
@@ -58,6 +62,10 @@ constexpr int kMsgAlpha = kPBytes;
 constexpr int kMsgL = kMsgAlpha + 512;
 constexpr int kMsgM = kMsgL + 512;
 constexpr int kMsgBytes = 18 * 1024;
+constexpr uint32_t kMsgTx = 128 * (8 * 16 + 3 * 4);  // bytes st.async delivers per message
+constexpr int kProdWarp0 = 4;
+constexpr int kProdThreads = 128;                    // warps 4-7
+constexpr int kMmaWarp = 8;
 
 constexpr int kTmemCols = 512;
 constexpr int kTmemS = 384;  // S buffers at columns 384 and 448 (Q uses columns [0, D_qk/2))
@@ -72,6 +80,7 @@ struct Hdr {
     int pad;
     float fin_l[128];
     float fin_m[128];
+    int32_t rowbuf[kKStages][kBK];  // physical rows of the tile being gathered into each stage
 };
 static_assert(sizeof(Hdr) <= 2048, "header must fit in 2 KiB");
 
@@ -82,6 +91,7 @@ constexpr int kSmemBytes = (kScoreSmem > kOutSmem ? kScoreSmem : kOutSmem) + 102
 
 struct TcArgs {
     const void *q;
+    const uint8_t *ori, *cmp;  // paged pools, rows of D_qk elements
     const int32_t *ori_bt, *tinfo, *rows;
     const float *sinks;
     void *out;
@@ -172,42 +182,68 @@ __device__ __forceinline__ int32_t key_row(const TcArgs &p, const Item &it, cons
     return r >= 0 ? r : oob;
 }
 
-// Producer warp: gathers `nch` 64-column slabs of 64 rows per tile into a ring.
-__device__ void producer(const TcArgs &p, const Sync &sy, const CUtensorMap *ori_map, const CUtensorMap *cmp_map,
-                         uint8_t *ring, uint64_t *full, uint64_t *empty, int stages, int nch) {
-    const int lane = threadIdx.x & 31;
-    uint32_t cnt = 0;
+// Producer warps 4-7: gather `nch` 128-byte slabs (nch = 8 or 9) of 64 rows
+// per tile into a ring with 16-byte cp.async, 128B-swizzled: 16-byte granule c
+// of row r lands at (c / 8) * 8 KiB + r * 128 + ((c % 8) ^ (r % 8)) * 16, the
+// UMMA K-major SW128 layout.  Thread pt owns granule pt % 64 of rows pt / 64,
+// +2, +4, ... (a warp reads 512 contiguous bytes of one row); with nch = 9 the
+// last 8 granules of every row are spread over all 128 threads.  A tile's full
+// barrier (count 128) completes once its copies have landed: each thread waits
+// for its own cp.async group one tile later, fences the async proxy, arrives.
+__device__ void producer(const TcArgs &p, const Sync &sy, uint8_t *ring, uint64_t *full, uint64_t *empty,
+                         int32_t (*rowbuf)[kBK], int stages, int nch) {
+    const int pt = threadIdx.x - kProdWarp0 * 32;
+    const size_t row_bytes = (size_t)p.Dq * 2;
     const uint32_t stage_bytes = (uint32_t)nch * kChunkBytes;
+    const int mc = pt & 63, mr = pt >> 6;         // main part: granule mc of rows mr + 2i
+    const int tc = 64 + (pt & 7), tr = pt >> 3;   // 9th slab: granule tc of rows tr + 16i
+    const uint32_t moff = (mc >> 3) * kChunkBytes, toff = 8 * kChunkBytes;
+    uint32_t cnt = 0, done = 0;
     for (int t = cluster_id_x(); t < p.T; t += ncluster_x()) {
         const Item it = load_item(p, t);
         const int32_t *crow = p.rows + (int64_t)t * p.row_cap;
-        for (int j = 0; j < it.ntiles; ++j, ++cnt) {
+        for (int j = 0; j < it.ntiles; ++j) {
             const int st = cnt % stages;
-            if (!wait_warp(sy, smem_u32(&empty[st]), ((cnt / stages) & 1) ^ 1)) return;
-            const bool win = j < it.nwt;
-            const int oob = win ? p.ori_rows : p.cmp_rows;
-            const int32_t ya = key_row(p, it, crow, j, 2 * lane, oob);
-            const int32_t yb = key_row(p, it, crow, j, 2 * lane + 1, oob);
-            const int g0 = (2 * lane) & 31, g1 = (2 * lane + 1) & 31;
-            const int32_t y0 = __shfl_sync(0xffffffffu, ya, g0), y1 = __shfl_sync(0xffffffffu, yb, g0);
-            const int32_t y2 = __shfl_sync(0xffffffffu, ya, g1), y3 = __shfl_sync(0xffffffffu, yb, g1);
-            const uint32_t bar = smem_u32(&full[st]);
-            if (lane == 0) mbar_arrive_expect_tx(bar, stage_bytes);
-            __syncwarp();
-            if (lane < 16) {
-                const uint32_t dst = smem_u32(ring + (size_t)st * stage_bytes) + lane * 512;
-                const CUtensorMap *map = win ? ori_map : cmp_map;
-                for (int c = 0; c < nch; ++c) tma_gather4(dst + c * kChunkBytes, map, c * 64, y0, y1, y2, y3, bar);
+            // all producer warps must agree before the named barrier below
+            const bool ok = wait_warp(sy, smem_u32(&empty[st]), ((cnt / stages) & 1) ^ 1);
+            if (!bar_red_and(2, kProdThreads, ok)) return;
+            if (pt < kBK) rowbuf[st][pt] = key_row(p, it, crow, j, pt, -1);
+            bar_sync(2, kProdThreads);
+            const uint8_t *pool = j < it.nwt ? p.ori : p.cmp;
+            const uint32_t dst0 = smem_u32(ring + (size_t)st * stage_bytes);
+#pragma unroll 8
+            for (int i = 0; i < kBK / 2; ++i) {
+                const int row = mr + 2 * i;
+                const int32_t r = rowbuf[st][row];
+                cp_async16(dst0 + moff + row * 128 + (((mc & 7) ^ (row & 7)) << 4),
+                           pool + (size_t)(r >= 0 ? r : 0) * row_bytes + mc * 16, r >= 0 ? 16u : 0u);
             }
-            __syncwarp();
+            if (nch == 9) {
+#pragma unroll
+                for (int i = 0; i < kBK / 16; ++i) {
+                    const int row = tr + 16 * i;
+                    const int32_t r = rowbuf[st][row];
+                    cp_async16(dst0 + toff + row * 128 + (((tc & 7) ^ (row & 7)) << 4),
+                               pool + (size_t)(r >= 0 ? r : 0) * row_bytes + tc * 16, r >= 0 ? 16u : 0u);
+                }
+            }
+            cp_async_commit();
+            ++cnt;
+            if (cnt - done > 1) {
+                cp_async_wait<1>();
+                fence_proxy_async_smem();
+                for (; done + 1 < cnt; ++done) mbar_arrive(smem_u32(&full[done % stages]));
+            }
         }
     }
+    cp_async_wait<0>();
+    fence_proxy_async_smem();
+    for (; done < cnt; ++done) mbar_arrive(smem_u32(&full[done % stages]));
 }
 
 template <bool kBF16>
 __global__ void __launch_bounds__(kThreads, 1)
-    fwd_tc_kernel(const TcArgs p, const __grid_constant__ CUtensorMap ori_map,
-                  const __grid_constant__ CUtensorMap cmp_map) {
+    fwd_tc_kernel(const TcArgs p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     Hdr *hd = reinterpret_cast<Hdr *>(smem);
@@ -218,7 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kKStages; ++i) {
-            mbar_init(smem_u32(&hd->k_full[i]), 1);
+            mbar_init(smem_u32(&hd->k_full[i]), kProdThreads);
             mbar_init(smem_u32(&hd->k_empty[i]), 1);
         }
         for (int i = 0; i < 2; ++i) {
@@ -228,10 +264,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(smem_u32(&hd->q_full), 4);
         for (int i = 0; i < kPStages; ++i) {
             mbar_init(smem_u32(&hd->p_empty[i]), 1);
-            mbar_init(smem_u32(&hd->p_full[i]), 4);
+            mbar_init(smem_u32(&hd->p_full[i]), 1);
         }
         for (int i = 0; i < kVStages; ++i) {
-            mbar_init(smem_u32(&hd->v_full[i]), 1);
+            mbar_init(smem_u32(&hd->v_full[i]), kProdThreads);
             mbar_init(smem_u32(&hd->v_empty[i]), 1);
         }
         mbar_init(smem_u32(&hd->o_full), 1);
@@ -242,9 +278,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(smem_u32(&hd->fin_ready), 1);
         hd->abort = 0;
         hd->rs_stage = 0;
+        // the output CTA expects the first message of each P stage (st.async complete_tx)
+        if (rank == 1)
+            for (int i = 0; i < kPStages; ++i) mbar_arrive_expect_tx(smem_u32(&hd->p_full[i]), kMsgTx);
         mbar_fence_init();
     }
-    if (warp == 1) {
+    if (warp == kMmaWarp) {
         tmem_alloc(smem_u32(&hd->tmem_base), kTmemCols);
         tmem_relinquish();
     }
@@ -259,9 +298,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ======================= score CTA =======================
         uint8_t *kbuf = data;
         const uint32_t kstage = (uint32_t)qch * kChunkBytes;
-        if (warp == 0) {
-            producer(p, sy, &ori_map, &cmp_map, kbuf, hd->k_full, hd->k_empty, kKStages, qch);
-        } else if (warp == 1) {
+        if (warp >= kProdWarp0 && warp < kProdWarp0 + 4) {
+            producer(p, sy, kbuf, hd->k_full, hd->k_empty, hd->rowbuf, kKStages, qch);
+        } else if (warp == kMmaWarp) {
             constexpr uint32_t idesc = idesc_f16(kBF16 ? 1u : 0u, 128, kBK, 0);
             uint32_t kc = 0, sc = 0, qc = 0;
             for (int t = cluster_id_x(); t < p.T; t += ncluster_x()) {
@@ -288,11 +327,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     __syncwarp();
                 }
             }
-        } else if (warp >= 4) {
-            const int h = threadIdx.x - 128;
-            const uint32_t lane_base = (uint32_t)((warp - 4) * 32) << 16;
+        } else if (warp < 4) {
+            const int h = threadIdx.x;
+            const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
             const uint32_t msg0 = map_to_cta(smem_u32(data + kVStages * vch * kChunkBytes), 1);
-            const uint32_t pfull0 = map_to_cta(smem_u32(&hd->p_full[0]), 1);
+            const uint32_t pfull0 = map_to_cta(smem_u32(&hd->p_full[0]), 1);  // the output CTA's barriers
             const float sink2 = h < p.N1 ? p.sinks[h] * 1.4426950408889634f : 0.f;
             uint32_t sc = 0, pc = 0;
             for (int t = cluster_id_x(); t < p.T; t += ncluster_x()) {
@@ -385,19 +424,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int ps = pc % kPStages;
                     if (!wait_warp(sy, smem_u32(&hd->p_empty[ps]), ((pc / kPStages) & 1) ^ 1, true)) goto done;
                     const uint32_t msg = msg0 + ps * kMsgBytes;
+                    const uint32_t pbar = pfull0 + ps * 8;
                     const uint32_t prow = msg + (h >> 3) * 1024 + (h & 7) * 128;
 #pragma unroll
                     for (int cc = 0; cc < 8; ++cc)
-                        st_cluster_v4(prow + ((cc ^ (h & 7)) << 4), pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2],
-                                      pk[4 * cc + 3]);
-                    st_cluster_u32(msg + kMsgAlpha + h * 4, __float_as_uint(alpha));
-                    if (last) {
-                        st_cluster_u32(msg + kMsgL + h * 4, __float_as_uint(lr));
-                        st_cluster_u32(msg + kMsgM + h * 4, __float_as_uint(m));
-                    }
-                    fence_proxy_async_all();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive_remote(pfull0 + ps * 8);
+                        st_async_v4(prow + ((cc ^ (h & 7)) << 4), pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2],
+                                    pk[4 * cc + 3], pbar);
+                    st_async_u32(msg + kMsgAlpha + h * 4, __float_as_uint(alpha), pbar);
+                    st_async_u32(msg + kMsgL + h * 4, __float_as_uint(lr), pbar);
+                    st_async_u32(msg + kMsgM + h * 4, __float_as_uint(m), pbar);
+                    (void)last;
                 }
                 if (p.lse && h < p.N1) p.lse[(int64_t)t * p.N1 + h] = (m + log2f(l)) * 0.6931471805599453f;
             }
@@ -414,9 +450,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t *vbuf = data;
         uint8_t *msgs = data + kVStages * vch * kChunkBytes;
         const uint32_t vstage = (uint32_t)vch * kChunkBytes;
-        if (warp == 0) {
-            producer(p, sy, &ori_map, &cmp_map, vbuf, hd->v_full, hd->v_empty, kVStages, vch);
-        } else if (warp == 1) {
+        if (warp >= kProdWarp0 && warp < kProdWarp0 + 4) {
+            producer(p, sy, vbuf, hd->v_full, hd->v_empty, hd->rowbuf, kVStages, vch);
+        } else if (warp == kMmaWarp) {
             const uint32_t nhalf = (uint32_t)p.Dv / 2;
             const uint32_t idesc = idesc_f16(kBF16 ? 1u : 0u, 128, nhalf, 1);
             uint32_t vc = 0, pc = 0, oc = 0, pvc = 0, rsc = 0;
@@ -428,6 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int j = 0; j < it.ntiles; ++j, ++vc, ++pc) {
                     const int ps = pc % kPStages, vs = vc % kVStages;
                     if (!wait_warp(sy, smem_u32(&hd->p_full[ps]), (pc / kPStages) & 1, true)) goto done;
+                    if (lane == 0) mbar_arrive_expect_tx(smem_u32(&hd->p_full[ps]), kMsgTx);  // next message
                     if (!wait_warp(sy, smem_u32(&hd->v_full[vs]), (vc / kVStages) & 1)) goto done;
                     uint8_t *msg = msgs + ps * kMsgBytes;
                     bool need = false;
@@ -479,9 +516,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     __syncwarp();
                 }
             }
-        } else if (warp >= 4) {
-            const int h = threadIdx.x - 128;
-            const uint32_t lane_base = (uint32_t)((warp - 4) * 32) << 16;
+        } else if (warp < 4) {
+            const int h = threadIdx.x;
+            const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
             uint32_t ofc = 0, rsc = 0, frc = 0;
             typedef typename std::conditional<kBF16, __nv_bfloat16, __half>::type OT;
             for (int t = cluster_id_x(); t < p.T; t += ncluster_x()) {
@@ -572,38 +609,7 @@ done:
     __syncthreads();
     cluster_sync();
     tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem, kTmemCols);
-}
-
-typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    if (!fn) {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(p);
-    }
-    return fn;
-}
-
-// Row-gather tensor map over a paged pool viewed as [rows, D] (box: 64 columns x 1 row, 128B swizzle).
-int make_map(CUtensorMap *map, const void *base, int64_t rows, int D, bool bf16) {
-    EncodeTiledFn fn = encode_fn();
-    if (!fn) return SAS_ERR_CUDA;
-    if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return SAS_ERR_INVALID_ARG;
-    cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)D * 2};
-    cuuint32_t box[2] = {64, 1};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-                    const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS ? SAS_OK : SAS_ERR_CUDA;
+    if (warp == kMmaWarp) tmem_dealloc(tmem, kTmemCols);
 }
 
 } // namespace
@@ -611,8 +617,10 @@ int make_map(CUtensorMap *map, const void *base, int64_t rows, int D, bool bf16)
 namespace sas_host {
 
 bool tc_supported(const SasFwdArgs &a) {
-    return a.num_heads >= 1 && a.num_heads <= 128 && a.head_dim % 64 == 0 && a.head_dim <= kMaxDq &&
-           a.v_head_dim % 128 == 0 && a.v_head_dim <= kMaxDv && a.v_head_dim <= a.head_dim;
+    // D_qk 512 (the reference paramsets) or 576 (DeepSeek-V4), D_v 512; the
+    // gather's thread map and the two N=256 PV halves are laid out for these.
+    return a.num_heads >= 1 && a.num_heads <= 128 && (a.head_dim == 512 || a.head_dim == 576) &&
+           a.v_head_dim == 512;
 }
 
 size_t tc_workspace(const SasFwdArgs &) { return 0; }
@@ -624,6 +632,8 @@ int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const 
     const bool bf16 = a.dtype == SAS_DTYPE_BF16;
     TcArgs p;
     p.q = q;
+    p.ori = static_cast<const uint8_t *>(ori_kv);
+    p.cmp = static_cast<const uint8_t *>(a.scenario >= 2 ? cmp_kv : ori_kv);
     p.ori_bt = ori_bt;
     p.tinfo = reinterpret_cast<const int32_t *>(ws + L.token_info);
     p.rows = reinterpret_cast<const int32_t *>(ws + L.cmp_rows);
@@ -642,12 +652,6 @@ int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const 
     p.ori_rows = a.ori_block_num * a.ori_block_size;
     p.cmp_rows = a.scenario >= 2 ? a.cmp_block_num * a.cmp_block_size : p.ori_rows;
     p.scale_log2 = a.softmax_scale * 1.4426950408889634f;
-    CUtensorMap ori_map, cmp_map;
-    int rc = make_map(&ori_map, ori_kv, p.ori_rows, a.head_dim, bf16);
-    if (rc) return rc;
-    rc = make_map(&cmp_map, a.scenario >= 2 ? cmp_kv : ori_kv, p.cmp_rows, a.head_dim, bf16);
-    if (rc) return rc;
-
     static bool attr_done[2] = {false, false};
     const int di = bf16 ? 0 : 1;
     if (!attr_done[di]) {
@@ -677,8 +681,7 @@ int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const 
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = bf16 ? cudaLaunchKernelEx(&cfg, fwd_tc_kernel<true>, p, ori_map, cmp_map)
-                         : cudaLaunchKernelEx(&cfg, fwd_tc_kernel<false>, p, ori_map, cmp_map);
+    cudaError_t e = bf16 ? cudaLaunchKernelEx(&cfg, fwd_tc_kernel<true>, p) : cudaLaunchKernelEx(&cfg, fwd_tc_kernel<false>, p);
     return check_cuda(e);
 }
 

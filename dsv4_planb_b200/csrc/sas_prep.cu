@@ -1,7 +1,7 @@
 // Key resolution: for every query token, its window bounds and the list of
 // physical compressed rows it attends to.
 //
-// One warp per (request b, query s < act_q[b]); the flat token row is
+// One CTA per (request b, query s < act_q[b]); the flat token row is
 // q_prefix[b] + s (kernel.py:421-474 decodes the same pair).  Semantics:
 //   window      keys [max(s_g - win_left, 0), s_g], s_g = act_kv - act_q + s
 //               (golden.py:125-131)
@@ -15,6 +15,10 @@
 // (table[b][p / bs] * bs + p % bs); an unmapped block gives -1, which the
 // attention kernels read as a zero row, as unpack_paged_kv (golden.py:247-268)
 // leaves unmapped blocks zero.
+//
+// The scan is data-parallel: each thread holds kPer consecutive slots, the
+// stop position is a block-wide minimum and the compaction a block-wide
+// exclusive prefix sum, so the kept rows keep their slot order.
 
 #include "sas_common.cuh"
 
@@ -28,25 +32,77 @@ struct PrepArgs {
     uint32_t *status;
 };
 
-constexpr int kWarps = 8;
+constexpr int kThreads = 256;
+constexpr int kTableSmem = 2048;  // block-table entries staged in shared memory
 
 __device__ __forceinline__ int floordiv_i(int a, int b) {
     int q = a / b, r = a % b;
     return (r != 0 && ((r < 0) != (b < 0))) ? q - 1 : q;
 }
 
-__global__ void __launch_bounds__(kWarps * 32) prep_kernel(PrepArgs p) {
-    const int lane = threadIdx.x & 31;
-    const int s = blockIdx.x * kWarps + (threadIdx.x >> 5);
+// Physical row of compressed position v of request b (table staged in smem when it fits).
+__device__ __forceinline__ int32_t cmp_row(const PrepArgs &p, const int32_t *tab_s, int b, int v) {
+    const int blk = v / p.cmp_block_size;
+    if (blk >= p.cmp_table_len) {
+        sas::set_status(p.status, SAS_STATUS_BAD_BLOCK);
+        return -1;
+    }
+    const int32_t phys = tab_s ? tab_s[blk] : __ldg(p.cmp_bt + (int64_t)b * p.cmp_table_len + blk);
+    if (phys < 0) {
+        if (phys != -1) sas::set_status(p.status, SAS_STATUS_BAD_BLOCK);
+        return -1;
+    }
+    if (phys >= p.cmp_block_num) {
+        sas::set_status(p.status, SAS_STATUS_BAD_BLOCK);
+        return -1;
+    }
+    return phys * p.cmp_block_size + (v - blk * p.cmp_block_size);
+}
+
+// Block-wide exclusive prefix sum of `v` (also returns the total).
+__device__ __forceinline__ int block_exscan(int v, int *total, int *warp_sums) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_sums[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int w = lane < kThreads / 32 ? warp_sums[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += y;
+        }
+        if (lane < kThreads / 32) warp_sums[lane] = w;  // inclusive per-warp totals
+    }
+    __syncthreads();
+    const int before = (warp > 0 ? warp_sums[warp - 1] : 0) + x - v;
+    *total = warp_sums[kThreads / 32 - 1];
+    __syncthreads();
+    return before;
+}
+
+template <int kPer>
+__global__ void __launch_bounds__(kThreads) prep_kernel(PrepArgs p) {
+    __shared__ int32_t tab_s[kTableSmem];
+    __shared__ int warp_sums[kThreads / 32];
+    __shared__ int s_stop;
+    __shared__ int s_bad;
+    const int s = blockIdx.x;
     const int b = blockIdx.y;
+    const int tid = threadIdx.x;
     if (b >= p.B) return;
     const int aq = __ldg(p.act_q + b);
-    if (s == 0 && lane == 0 && aq > p.max_q_len) sas::set_status(p.status, SAS_STATUS_BAD_TOKEN);
+    if (s == 0 && tid == 0 && aq > p.max_q_len) sas::set_status(p.status, SAS_STATUS_BAD_TOKEN);
     if (s >= aq) return;
     const int akv = __ldg(p.act_kv + b);
     const int64_t t = (int64_t)__ldg(p.q_prefix + b) + s;
     if (t < 0 || t >= p.T) {
-        if (lane == 0) sas::set_status(p.status, SAS_STATUS_BAD_TOKEN);
+        if (tid == 0) sas::set_status(p.status, SAS_STATUS_BAD_TOKEN);
         return;
     }
     const int s_g = akv - aq + s;
@@ -58,39 +114,59 @@ __global__ void __launch_bounds__(kWarps * 32) prep_kernel(PrepArgs p) {
     int n_cmp = 0;
     int32_t *rows = p.rows + t * (int64_t)p.row_cap;
     if (p.scenario >= 2) {
+        const bool staged = p.cmp_table_len <= kTableSmem;
+        if (staged)
+            for (int i = tid; i < p.cmp_table_len; i += kThreads) tab_s[i] = __ldg(p.cmp_bt + (int64_t)b * p.cmp_table_len + i);
+        if (tid == 0) {
+            s_stop = 0x7fffffff;
+            s_bad = 0;
+        }
+        __syncthreads();
+        const int32_t *tab = staged ? tab_s : nullptr;
         const int thr = floordiv_i(akv - aq + s + 1, p.ratio);
         if (p.scenario == 2) {
-            if (thr > p.row_cap && lane == 0) sas::set_status(p.status, SAS_STATUS_BAD_TOKEN);
-            const int n = min(max(thr, 0), p.row_cap);
-            for (int i = lane; i < n; i += 32)
-                rows[i] = (int32_t)sas::paged_row(p.cmp_bt, b, p.cmp_table_len, p.cmp_block_size, p.cmp_block_num,
-                                                  i, p.status);
-            n_cmp = n;
+            if (thr > p.row_cap && tid == 0) sas::set_status(p.status, SAS_STATUS_BAD_TOKEN);
+            n_cmp = min(max(thr, 0), p.row_cap);
+            for (int i = tid; i < n_cmp; i += kThreads) rows[i] = cmp_row(p, tab, b, i);
         } else {
             const int n_scan = min(p.K, thr);
             const int32_t *ir = p.idx + t * (int64_t)p.K;
-            bool bad = false;
-            for (int base = 0; base < n_scan; base += 32) {
-                const int i = base + lane;
-                const int v = i < n_scan ? __ldg(ir + i) : 0;
-                const unsigned stop = __ballot_sync(0xffffffffu, i < n_scan && v == -1);
-                const int stop_lane = stop ? __ffs(stop) - 1 : 32;
-                const bool live = i < n_scan && lane < stop_lane;
-                bad |= live && v < -1;
-                const bool keep = live && v >= 0 && v < thr;
-                const unsigned km = __ballot_sync(0xffffffffu, keep);
-                if (keep) {
-                    const int slot = n_cmp + __popc(km & ((1u << lane) - 1u));
-                    rows[slot] = (int32_t)sas::paged_row(p.cmp_bt, b, p.cmp_table_len, p.cmp_block_size,
-                                                         p.cmp_block_num, v, p.status);
+            // process the scan window in chunks of kThreads * kPer slots
+            for (int base = 0; base < n_scan; base += kThreads * kPer) {
+                int v[kPer];
+                const int i0 = base + tid * kPer;
+                int first_stop = 0x7fffffff;
+#pragma unroll
+                for (int k = 0; k < kPer; ++k) {
+                    v[k] = i0 + k < n_scan ? __ldg(ir + i0 + k) : 0;
+                    if (i0 + k < n_scan && v[k] == -1 && first_stop == 0x7fffffff) first_stop = i0 + k;
                 }
-                n_cmp += __popc(km);
-                if (stop) break;
+                if (first_stop != 0x7fffffff) atomicMin(&s_stop, first_stop);
+                __syncthreads();
+                const int stop = min(s_stop, n_scan);
+                int cnt = 0;
+                bool bad = false;
+#pragma unroll
+                for (int k = 0; k < kPer; ++k) {
+                    const bool live = i0 + k < stop;
+                    bad |= live && v[k] < -1;
+                    cnt += (live && v[k] >= 0 && v[k] < thr) ? 1 : 0;
+                }
+                if (bad) s_bad = 1;
+                int total;
+                int pos = n_cmp + block_exscan(cnt, &total, warp_sums);
+#pragma unroll
+                for (int k = 0; k < kPer; ++k) {
+                    if (i0 + k < stop && v[k] >= 0 && v[k] < thr) rows[pos++] = cmp_row(p, tab, b, v[k]);
+                }
+                n_cmp += total;
+                if (stop < n_scan) break;  // uniform: s_stop is shared
             }
-            if (__any_sync(0xffffffffu, bad) && lane == 0) sas::set_status(p.status, SAS_STATUS_BAD_INDEX);
+            __syncthreads();
+            if (tid == 0 && s_bad) sas::set_status(p.status, SAS_STATUS_BAD_INDEX);
         }
     }
-    if (lane == 0) {
+    if (tid == 0) {
         int32_t *ti = p.tinfo + t * sas::TI_INTS;
         ti[sas::TI_B] = b;
         ti[sas::TI_SGLOBAL] = s_g;
@@ -136,8 +212,9 @@ int launch_prep(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const in
     p.tinfo = reinterpret_cast<int32_t *>(ws + L.token_info);
     p.rows = reinterpret_cast<int32_t *>(ws + L.cmp_rows);
     p.status = reinterpret_cast<uint32_t *>(ws + L.status);
-    dim3 grid((a.max_q_len + kWarps - 1) / kWarps, a.batch);
-    prep_kernel<<<grid, kWarps * 32, 0, s>>>(p);
+    dim3 grid(a.max_q_len, a.batch);
+    if (a.scenario == 3 && a.topk > kThreads * 4) prep_kernel<8><<<grid, kThreads, 0, s>>>(p);
+    else prep_kernel<4><<<grid, kThreads, 0, s>>>(p);
     return check_cuda(cudaGetLastError());
 }
 

@@ -106,8 +106,43 @@ __device__ __forceinline__ bool bar_red_or(int id, int count, bool v) {
         : "memory");
     return r != 0;
 }
+__device__ __forceinline__ bool bar_red_and(int id, int count, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "r"(id), "r"(count)
+        : "memory");
+    return r != 0;
+}
 __device__ __forceinline__ void bar_sync(int id, int count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// ---- cp.async (16 bytes, L2 only); src_size 0 writes zeros ------------------------
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_size) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_size) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// ---- remote stores that complete-tx an mbarrier of the destination CTA ----------
+__device__ __forceinline__ void st_async_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d,
+                                            uint32_t cluster_bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                     addr),
+                 "r"(a), "r"(b), "r"(c), "r"(d), "r"(cluster_bar)
+                 : "memory");
+}
+__device__ __forceinline__ void st_async_u32(uint32_t addr, uint32_t v, uint32_t cluster_bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(addr), "r"(v),
+                 "r"(cluster_bar)
+                 : "memory");
 }
 
 // ---- TMA: four rows of a 2-D tensor map into shared memory --------------------
