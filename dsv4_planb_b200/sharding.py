@@ -1,0 +1,118 @@
+"""Request sharding of one decode batch across the GPUs of a node.
+
+Requests are independent (SURVEY: the path has no exchange step), so each
+rank runs ``sparse_attn_sharedkv`` on its own subset of requests over its own
+slice of the paged pools, with block ids remapped to that slice.  NCCL is used
+only to bring outputs back together for verification.
+
+* ``partition_requests``  greedy LPT over a per-request cost (window keys plus
+  compressed keys; by default ``min(128, kv) + min(topk, kv // ratio)`` per
+  query token), so ranks get equal work rather than equal counts;
+* ``shard_workload``      the rank's sub-workload: its requests' query rows,
+  indices, lengths, and the physical blocks its block tables reference,
+  compacted into a local pool with remapped tables;
+* ``gather_outputs``      ``all_gather`` of every rank's (out, lse, request ids)
+  padded to a common size, reassembled in the original token order.
+"""
+
+from __future__ import annotations
+
+import heapq
+from typing import List, Sequence
+
+import torch
+
+from .workloads import Workload
+
+
+def request_costs(q_lens: Sequence[int], kv_lens: Sequence[int], topk: int, cmp_ratio: int = 4,
+                  win: int = 128) -> List[int]:
+    costs = []
+    for ql, kv in zip(q_lens, kv_lens):
+        c = 0
+        for s in range(ql):
+            sg = kv - ql + s
+            c += min(win, max(sg + 1, 0)) + min(topk, max((sg + 1) // cmp_ratio, 0))
+        costs.append(c)
+    return costs
+
+
+def partition_requests(costs: Sequence[int], world: int) -> List[List[int]]:
+    """Longest-processing-time assignment of requests to ``world`` ranks (each list sorted)."""
+    heap = [(0, r) for r in range(world)]
+    heapq.heapify(heap)
+    parts: List[List[int]] = [[] for _ in range(world)]
+    for b in sorted(range(len(costs)), key=lambda i: (-costs[i], i)):
+        load, r = heapq.heappop(heap)
+        parts[r].append(b)
+        heapq.heappush(heap, (load + costs[b], r))
+    return [sorted(p) for p in parts]
+
+
+def _compact_pool(pool: torch.Tensor, table: torch.Tensor):
+    """Copy the blocks ``table`` references into a new pool; return it and the remapped table."""
+    used = table[table >= 0].unique(sorted=True)
+    remap = torch.full((pool.shape[0],), -1, dtype=torch.int32, device=table.device)
+    remap[used.long()] = torch.arange(used.numel(), dtype=torch.int32, device=table.device)
+    new_table = torch.where(table >= 0, remap[table.clamp(min=0).long()], table)
+    new_pool = pool[used.long()] if used.numel() else pool[:1]
+    return new_pool.contiguous(), new_table.contiguous()
+
+
+def shard_workload(wl: Workload, requests: Sequence[int]) -> Workload:
+    """The sub-workload of ``requests`` (original request ids, ascending)."""
+    cu = wl.cu_seqlens_q.tolist()
+    rows = [t for b in requests for t in range(cu[b], cu[b + 1])]
+    row_idx = torch.tensor(rows, dtype=torch.long, device=wl.q.device)
+    req_idx = torch.tensor(list(requests), dtype=torch.long, device=wl.q.device)
+    q_lens = [wl.q_lens[b] for b in requests]
+    kv_lens = [wl.kv_lens[b] for b in requests]
+    ori_kv, ori_bt = _compact_pool(wl.ori_kv, wl.ori_block_table[req_idx])
+    cmp_kv = cmp_bt = None
+    if wl.cmp_kv is not None:
+        cmp_kv, cmp_bt = _compact_pool(wl.cmp_kv, wl.cmp_block_table[req_idx])
+    cu_new = torch.zeros(len(requests) + 1, dtype=torch.int32, device=wl.q.device)
+    if q_lens:
+        cu_new[1:] = torch.tensor(q_lens, dtype=torch.int32, device=wl.q.device).cumsum(0)
+    return Workload(
+        name=f"{wl.name}[shard]", q=wl.q[row_idx].contiguous(), ori_kv=ori_kv, ori_block_table=ori_bt, cmp_kv=cmp_kv,
+        cmp_block_table=cmp_bt,
+        cmp_sparse_indices=None if wl.cmp_sparse_indices is None else wl.cmp_sparse_indices[row_idx].contiguous(),
+        cu_seqlens_q=cu_new, seqused_kv=wl.seqused_kv[req_idx].contiguous(), sinks=wl.sinks,
+        softmax_scale=wl.softmax_scale, cmp_ratio=wl.cmp_ratio, topk=wl.topk, v_head_dim=wl.v_head_dim,
+        ori_win_left=wl.ori_win_left, q_lens=q_lens, kv_lens=kv_lens)
+
+
+def gather_outputs(out: torch.Tensor, lse: torch.Tensor, requests: Sequence[int], q_lens_all: Sequence[int],
+                   group=None):
+    """Reassemble every rank's outputs in the original flat token order (collective)."""
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    dev = out.device
+    cu = [0]
+    for ql in q_lens_all:
+        cu.append(cu[-1] + ql)
+    rows = torch.tensor([t for b in requests for t in range(cu[b], cu[b + 1])], dtype=torch.long, device=dev)
+    n = torch.tensor([rows.numel()], dtype=torch.long, device=dev)
+    sizes = [torch.zeros_like(n) for _ in range(world)]
+    dist.all_gather(sizes, n, group=group)
+    cap = int(max(int(s.item()) for s in sizes))
+    pad = cap - rows.numel()
+    o = torch.cat([out.float(), out.new_zeros((pad,) + tuple(out.shape[1:])).float()]) if pad else out.float()
+    l_ = torch.cat([lse, lse.new_zeros((pad, lse.shape[1]))]) if pad else lse
+    r = torch.cat([rows, rows.new_full((pad,), -1)]) if pad else rows
+    os_ = [torch.empty_like(o) for _ in range(world)]
+    ls_ = [torch.empty_like(l_) for _ in range(world)]
+    rs_ = [torch.empty_like(r) for _ in range(world)]
+    dist.all_gather(os_, o.contiguous(), group=group)
+    dist.all_gather(ls_, l_.contiguous(), group=group)
+    dist.all_gather(rs_, r.contiguous(), group=group)
+    T = cu[-1]
+    full_o = torch.zeros((T,) + tuple(out.shape[1:]), dtype=torch.float32, device=dev)
+    full_l = torch.zeros((T, lse.shape[1]), dtype=lse.dtype, device=dev)
+    for o_i, l_i, r_i in zip(os_, ls_, rs_):
+        keep = r_i >= 0
+        full_o[r_i[keep]] = o_i[keep]
+        full_l[r_i[keep]] = l_i[keep]
+    return full_o, full_l
