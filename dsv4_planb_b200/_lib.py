@@ -25,6 +25,8 @@ SAS_STATUS_NO_PROGRESS = 0x4
 SAS_STATUS_WAIT_TIMEOUT = 0x8
 SAS_STATUS_BAD_TOKEN = 0x10
 
+SAS_NOALLOC_SCRATCH_BYTES = 16 << 20
+
 SAS_DTYPE_BF16 = 0
 SAS_DTYPE_FP16 = 1
 
@@ -36,6 +38,7 @@ LAYOUT_KV = {"PA_ND": 0, "TND": 1}
 EXPORTS = (
     "sas_workspace_size",
     "sas_forward",
+    "sas_forward_noalloc",
     "sas_resolve_rows",
     "sas_read_status",
     "sas_set_kernel_events",
@@ -111,6 +114,7 @@ _SZ = ctypes.c_size_t
 _SIGNATURES = {
     "sas_workspace_size": (ctypes.c_int, [ctypes.POINTER(SasFwdArgs), ctypes.POINTER(_SZ)]),
     "sas_forward": (ctypes.c_int, [ctypes.POINTER(SasFwdArgs)] + [_P] * 13 + [_P, _SZ, _P]),
+    "sas_forward_noalloc": (ctypes.c_int, [ctypes.POINTER(SasFwdArgs)] + [_P] * 13 + [_P]),
     "sas_resolve_rows": (ctypes.c_int, [ctypes.POINTER(SasFwdArgs)] + [_P] * 8 + [_P, _SZ, _P]),
     "sas_read_status": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_uint32), _P]),
     "sas_set_kernel_events": (ctypes.c_int, [_P, _P]),

@@ -124,6 +124,32 @@ int sas_resolve_rows(const SasFwdArgs *args, const int32_t *ori_block_table, con
  */
 int sas_read_status(const void *workspace, uint32_t *status, void *stream);
 
+/*
+ * sas_forward for callers that cannot allocate device memory.  Some hosts of
+ * this operator own every byte of the GPU and forbid device allocations once
+ * they are running -- a serving engine that reserves nearly all of HBM for its
+ * paged KV pool up front, or a thin FFI host (ctypes, cgo) that embeds the op
+ * with no device allocator of its own -- so they cannot provide the workspace
+ * sas_forward asks for.  This entry point takes the same arguments minus the
+ * workspace and uses a scratch array compiled into the library instead
+ * (SAS_NOALLOC_SCRATCH_BYTES per GPU that loads the library, held until the
+ * process exits).  It allocates nothing: no cudaMalloc, no cudaFree.
+ *   - Calls whose sas_workspace_size exceeds SAS_NOALLOC_SCRATCH_BYTES are
+ *     rejected with SAS_ERR_WORKSPACE (use sas_forward for those).
+ *   - The first call on a device looks up the array's device address on the
+ *     current device; make that first call before any stream capture.
+ *   - Every call shares the one array: calls that overlap on the GPU (other
+ *     streams, other host threads) race.  Serialise them on one stream.
+ *   - sas_read_status cannot be used with it (the status word lives in the
+ *     private scratch).
+ * No counterpart in the reference.
+ */
+#define SAS_NOALLOC_SCRATCH_BYTES (16u << 20)
+int sas_forward_noalloc(const SasFwdArgs *args, const void *q, const void *ori_kv, const int32_t *ori_block_table,
+                        const void *cmp_kv, const int32_t *cmp_block_table, const int32_t *cmp_indices,
+                        const int32_t *q_prefix, const int32_t *act_q_len, const int32_t *act_kv_len,
+                        const float *sinks, const int32_t *metadata, void *out, float *lse, void *stream);
+
 /* ---- metadata scheduler ----------------------------------------------------
  * Replaces sparse_attn_sharedkv_metadata (metadata.py:1018-1086, the Python
  * port of the aicpu SparseAttnSharedkvMetadata op) with a CUDA kernel whose
