@@ -22,8 +22,7 @@
 //
 // Keys of a token are its window rows (padded to a multiple of 64) followed by
 // its resolved compressed rows (sas_prep.cu); masked / unmapped rows are read
-// as zeros (cp.async with source size 0).  (TMA tile::gather4 was measured at
-// ~40 ns per 512-byte gather per SM here, too slow to feed the tensor cores.)  Scores live in the
+// as zeros (cp.async with source size 0).  Scores live in the
 // log2 domain.  The running max is only raised when a tile's max exceeds it by
 // more than 8 (P <= 2^8, exact in bf16 and fp32), so O is rarely rescaled; the
 // final out = O / l and lse = (m + log2 l) ln 2 equal the reference golden
@@ -80,7 +79,7 @@ struct Hdr {
     int pad;
     float fin_l[128];
     float fin_m[128];
-    int32_t rowbuf[kKStages][kBK];  // physical rows of the tile being gathered into each stage
+    alignas(16) int32_t rowbuf[kKStages][kBK];  // physical rows of the tile gathered into each stage
 };
 static_assert(sizeof(Hdr) <= 2048, "header must fit in 2 KiB");
 
@@ -166,20 +165,38 @@ __device__ __forceinline__ bool poll_warp(uint32_t bar, uint32_t parity) {
     return true;
 }
 
-// Physical row of key k of tile j of an item, or `oob` (reads as zeros).
-__device__ __forceinline__ int32_t key_row(const TcArgs &p, const Item &it, const int32_t *crow, int j, int k,
-                                           int oob) {
+// Row lookup of key k of tile j of an item, split in two so that the global
+// load (a block-table entry for window keys, a resolved row for compressed
+// keys) is issued one tile ahead and its latency hides behind the copies of
+// the current tile.  key_fetch issues the load; key_row turns its value into
+// the physical row, or -1 (masked / unmapped: read as zeros).
+__device__ __forceinline__ int32_t key_fetch(const TcArgs &p, const Item &it, const int32_t *crow, int j, int k) {
     if (j < it.nwt) {
         const int slot = j * kBK + k;
-        if (slot >= it.n_win) return oob;
-        const int64_t r = sas::paged_row(p.ori_bt, it.b, p.ori_table_len, p.ori_block_size, p.ori_block_num,
-                                         (int64_t)it.left + slot, p.status);
-        return r >= 0 ? (int32_t)r : oob;
+        if (slot >= it.n_win) return -1;
+        const int64_t blk = ((int64_t)it.left + slot) / p.ori_block_size;
+        if (it.left + slot < 0 || blk >= p.ori_table_len) return -1;
+        return __ldg(p.ori_bt + (int64_t)it.b * p.ori_table_len + blk);
     }
     const int c = (j - it.nwt) * kBK + k;
-    if (c >= it.n_cmp) return oob;
-    const int32_t r = crow[c];
-    return r >= 0 ? r : oob;
+    return c < it.n_cmp ? __ldg(crow + c) : -1;
+}
+
+__device__ __forceinline__ int32_t key_row(const TcArgs &p, const Item &it, int j, int k, int32_t fetched) {
+    if (j < it.nwt) {
+        const int slot = j * kBK + k;
+        if (slot >= it.n_win) return -1;
+        const int64_t pos = (int64_t)it.left + slot;
+        if (pos < 0) return -1;
+        const int64_t blk = pos / p.ori_block_size;
+        if (blk >= p.ori_table_len || (fetched < 0 && fetched != -1) || fetched >= p.ori_block_num) {
+            sas::set_status(p.status, SAS_STATUS_BAD_BLOCK);
+            return -1;
+        }
+        if (fetched < 0) return -1;
+        return (int32_t)((int64_t)fetched * p.ori_block_size + (pos - blk * p.ori_block_size));
+    }
+    return fetched >= 0 ? fetched : -1;
 }
 
 // Producer warps 4-7: gather `nch` 128-byte slabs (nch = 8 or 9) of 64 rows
@@ -188,8 +205,11 @@ __device__ __forceinline__ int32_t key_row(const TcArgs &p, const Item &it, cons
 // UMMA K-major SW128 layout.  Thread pt owns granule pt % 64 of rows pt / 64,
 // +2, +4, ... (a warp reads 512 contiguous bytes of one row); with nch = 9 the
 // last 8 granules of every row are spread over all 128 threads.  A tile's full
-// barrier (count 128) completes once its copies have landed: each thread waits
-// for its own cp.async group one tile later, fences the async proxy, arrives.
+// barrier (count 128) completes when every thread's copies for it have landed
+// (cp.async.mbarrier.arrive.noinc), so the MMA can start on it at once.  The
+// row lookups of the next tile load while this tile's copies issue.
+// (Measured here and not faster: TMA tile::gather4 from these 128 threads,
+// cp.async and gather4 sharing the slabs, an L2 prefetch warp 1-5 tiles ahead.)
 __device__ void producer(const TcArgs &p, const Sync &sy, uint8_t *ring, uint64_t *full, uint64_t *empty,
                          int32_t (*rowbuf)[kBK], int stages, int nch) {
     const int pt = threadIdx.x - kProdWarp0 * 32;
@@ -198,17 +218,18 @@ __device__ void producer(const TcArgs &p, const Sync &sy, uint8_t *ring, uint64_
     const int mc = pt & 63, mr = pt >> 6;         // main part: granule mc of rows mr + 2i
     const int tc = 64 + (pt & 7), tr = pt >> 3;   // 9th slab: granule tc of rows tr + 16i
     const uint32_t moff = (mc >> 3) * kChunkBytes, toff = 8 * kChunkBytes;
-    uint32_t cnt = 0, done = 0;
+    uint32_t cnt = 0;
     for (int t = cluster_id_x(); t < p.T; t += ncluster_x()) {
         const Item it = load_item(p, t);
         const int32_t *crow = p.rows + (int64_t)t * p.row_cap;
+        int32_t fetched = pt < kBK && it.ntiles > 0 ? key_fetch(p, it, crow, 0, pt) : -1;
         for (int j = 0; j < it.ntiles; ++j) {
             const int st = cnt % stages;
-            // all producer warps must agree before the named barrier below
             const bool ok = wait_warp(sy, smem_u32(&empty[st]), ((cnt / stages) & 1) ^ 1);
+            if (ok && pt < kBK) rowbuf[st][pt] = key_row(p, it, j, pt, fetched);
+            // all producer warps agree (abort) and see the tile's rows
             if (!bar_red_and(2, kProdThreads, ok)) return;
-            if (pt < kBK) rowbuf[st][pt] = key_row(p, it, crow, j, pt, -1);
-            bar_sync(2, kProdThreads);
+            if (pt < kBK && j + 1 < it.ntiles) fetched = key_fetch(p, it, crow, j + 1, pt);
             const uint8_t *pool = j < it.nwt ? p.ori : p.cmp;
             const uint32_t dst0 = smem_u32(ring + (size_t)st * stage_bytes);
 #pragma unroll 8
@@ -227,18 +248,11 @@ __device__ void producer(const TcArgs &p, const Sync &sy, uint8_t *ring, uint64_
                                pool + (size_t)(r >= 0 ? r : 0) * row_bytes + tc * 16, r >= 0 ? 16u : 0u);
                 }
             }
-            cp_async_commit();
+            // the stage barrier (count 128) gets this thread's arrival when its copies land
+            cp_async_mbar_arrive_noinc(smem_u32(&full[st]));
             ++cnt;
-            if (cnt - done > 1) {
-                cp_async_wait<1>();
-                fence_proxy_async_smem();
-                for (; done + 1 < cnt; ++done) mbar_arrive(smem_u32(&full[done % stages]));
-            }
         }
     }
-    cp_async_wait<0>();
-    fence_proxy_async_smem();
-    for (; done < cnt; ++done) mbar_arrive(smem_u32(&full[done % stages]));
 }
 
 template <bool kBF16>
@@ -312,6 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int j = 0; j < it.ntiles; ++j, ++kc, ++sc) {
                     const int ks = kc % kKStages, sb = sc & 1;
                     if (!wait_warp(sy, smem_u32(&hd->k_full[ks]), (kc / kKStages) & 1)) goto done;
+                    fence_proxy_async_smem();  // cp.async (generic proxy) writes -> UMMA reads
                     if (!wait_warp(sy, smem_u32(&hd->s_free[sb]), ((sc >> 1) & 1) ^ 1)) goto done;
                     tc_fence_after();
                     if (lane == 0) {
@@ -466,6 +481,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (!wait_warp(sy, smem_u32(&hd->p_full[ps]), (pc / kPStages) & 1, true)) goto done;
                     if (lane == 0) mbar_arrive_expect_tx(smem_u32(&hd->p_full[ps]), kMsgTx);  // next message
                     if (!wait_warp(sy, smem_u32(&hd->v_full[vs]), (vc / kVStages) & 1)) goto done;
+                    fence_proxy_async_smem();
                     uint8_t *msg = msgs + ps * kMsgBytes;
                     bool need = false;
                     for (int i = lane; i < 128; i += 32)
