@@ -8,9 +8,9 @@
 //   TMEM: Q (A operand, D_qk/2 cols)         TMEM: O (128 x D_v fp32)
 //         S double buffer (2 x 64 cols)
 //   warps 4-7 gather 64 K rows (all D_qk     warps 4-7 gather 64 V rows (first D_v
-//           columns) per tile: 16-byte               columns) per tile
-//           cp.async into the 128B-swizzled
-//           UMMA layout
+//           columns) per tile: TMA                   columns) per tile
+//           tile::gather4 into the 128B-
+//           swizzled UMMA layout
 //   warp 8  tcgen05.mma  S = Q K^T           warp 8  tcgen05.mma  O += P V
 //           (M=128 heads, N=64 keys)                 (M=128 heads, N=D_v/2, 2 halves)
 //   warps 0-3 softmax: thread = head         warps 0-3 rescale O rows on request;
@@ -22,7 +22,7 @@
 //
 // Keys of a token are its window rows (padded to a multiple of 64) followed by
 // its resolved compressed rows (sas_prep.cu); masked / unmapped rows are read
-// as zeros (cp.async with source size 0).  Scores live in the
+// as zeros (the gather points them past the pool).  Scores live in the
 // log2 domain.  The running max is only raised when a tile's max exceeds it by
 // more than 8 (P <= 2^8, exact in bf16 and fp32), so O is rarely rescaled; the
 // final out = O / l and lse = (m + log2 l) ln 2 equal the reference golden
@@ -199,25 +199,25 @@ __device__ __forceinline__ int32_t key_row(const TcArgs &p, const Item &it, int 
     return fetched >= 0 ? fetched : -1;
 }
 
-// Producer warps 4-7: gather `nch` 128-byte slabs (nch = 8 or 9) of 64 rows
-// per tile into a ring with 16-byte cp.async, 128B-swizzled: 16-byte granule c
-// of row r lands at (c / 8) * 8 KiB + r * 128 + ((c % 8) ^ (r % 8)) * 16, the
-// UMMA K-major SW128 layout.  Thread pt owns granule pt % 64 of rows pt / 64,
-// +2, +4, ... (a warp reads 512 contiguous bytes of one row); with nch = 9 the
-// last 8 granules of every row are spread over all 128 threads.  A tile's full
-// barrier (count 128) completes when every thread's copies for it have landed
-// (cp.async.mbarrier.arrive.noinc), so the MMA can start on it at once.  The
+// Producer warps 4-7: gather `nch` 128-byte slabs (nch = 8 or 9; slab c =
+// columns 64c .. 64c+63) of the tile's 64 rows into a ring stage with TMA
+// tile::gather4 (4 rows x 128 bytes per copy), in the UMMA K-major SW128
+// layout the tensor map's swizzle produces: row r of slab c at c * 8 KiB +
+// r * 128, 16-byte granule g at (g ^ r % 8) * 16.  Thread pt issues the copy
+// of slab pt / 16, rows 4 (pt % 16) .. +3 (and, with nch = 9, threads 0-15 the
+// ninth slab's); masked rows point one past the pool and read zeros.  Thread 0
+// arms the stage's full barrier with the tile's byte count before the
+// producer barrier, so every copy's complete_tx lands on an armed phase.  The
 // row lookups of the next tile load while this tile's copies issue.
-// (Measured here and not faster: TMA tile::gather4 from these 128 threads,
-// cp.async and gather4 sharing the slabs, an L2 prefetch warp 1-5 tiles ahead.)
-__device__ void producer(const TcArgs &p, const Sync &sy, uint8_t *ring, uint64_t *full, uint64_t *empty,
-                         int32_t (*rowbuf)[kBK], int stages, int nch) {
+//
+// Measured on the c2 decode batch: the score CTA's gather bounds the kernel.
+// Per SM, TMA gather4 sustains more random-row ingest than 16-byte cp.async
+// (~40 vs ~30 GB/s in isolation; 113 vs 121 us for the kernel).
+__device__ void producer(const TcArgs &p, const Sync &sy, const CUtensorMap *ori_map, const CUtensorMap *cmp_map,
+                         uint8_t *ring, uint64_t *full, uint64_t *empty, int32_t (*rowbuf)[kBK], int stages, int nch) {
     const int pt = threadIdx.x - kProdWarp0 * 32;
-    const size_t row_bytes = (size_t)p.Dq * 2;
+    const int slab = pt >> 4, quad = pt & 15;
     const uint32_t stage_bytes = (uint32_t)nch * kChunkBytes;
-    const int mc = pt & 63, mr = pt >> 6;         // main part: granule mc of rows mr + 2i
-    const int tc = 64 + (pt & 7), tr = pt >> 3;   // 9th slab: granule tc of rows tr + 16i
-    const uint32_t moff = (mc >> 3) * kChunkBytes, toff = 8 * kChunkBytes;
     uint32_t cnt = 0;
     for (int t = cluster_id_x(); t < p.T; t += ncluster_x()) {
         const Item it = load_item(p, t);
@@ -225,31 +225,23 @@ __device__ void producer(const TcArgs &p, const Sync &sy, uint8_t *ring, uint64_
         int32_t fetched = pt < kBK && it.ntiles > 0 ? key_fetch(p, it, crow, 0, pt) : -1;
         for (int j = 0; j < it.ntiles; ++j) {
             const int st = cnt % stages;
+            const uint32_t fb = smem_u32(&full[st]);
             const bool ok = wait_warp(sy, smem_u32(&empty[st]), ((cnt / stages) & 1) ^ 1);
             if (ok && pt < kBK) rowbuf[st][pt] = key_row(p, it, j, pt, fetched);
+            if (ok && pt == 0) mbar_arrive_expect_tx(fb, stage_bytes);
             // all producer warps agree (abort) and see the tile's rows
             if (!bar_red_and(2, kProdThreads, ok)) return;
             if (pt < kBK && j + 1 < it.ntiles) fetched = key_fetch(p, it, crow, j + 1, pt);
-            const uint8_t *pool = j < it.nwt ? p.ori : p.cmp;
-            const uint32_t dst0 = smem_u32(ring + (size_t)st * stage_bytes);
-#pragma unroll 8
-            for (int i = 0; i < kBK / 2; ++i) {
-                const int row = mr + 2 * i;
-                const int32_t r = rowbuf[st][row];
-                cp_async16(dst0 + moff + row * 128 + (((mc & 7) ^ (row & 7)) << 4),
-                           pool + (size_t)(r >= 0 ? r : 0) * row_bytes + mc * 16, r >= 0 ? 16u : 0u);
-            }
-            if (nch == 9) {
-#pragma unroll
-                for (int i = 0; i < kBK / 16; ++i) {
-                    const int row = tr + 16 * i;
-                    const int32_t r = rowbuf[st][row];
-                    cp_async16(dst0 + toff + row * 128 + (((tc & 7) ^ (row & 7)) << 4),
-                               pool + (size_t)(r >= 0 ? r : 0) * row_bytes + tc * 16, r >= 0 ? 16u : 0u);
-                }
-            }
-            // the stage barrier (count 128) gets this thread's arrival when its copies land
-            cp_async_mbar_arrive_noinc(smem_u32(&full[st]));
+            const bool win = j < it.nwt;
+            const int32_t oob = win ? p.ori_rows : p.cmp_rows;
+            const CUtensorMap *map = win ? ori_map : cmp_map;
+            const uint32_t base = smem_u32(ring + (size_t)st * stage_bytes);
+            const int4 r4 = reinterpret_cast<const int4 *>(rowbuf[st])[quad];
+            const int y0 = r4.x >= 0 ? r4.x : oob, y1 = r4.y >= 0 ? r4.y : oob, y2 = r4.z >= 0 ? r4.z : oob,
+                      y3 = r4.w >= 0 ? r4.w : oob;
+            tma_gather4(base + slab * kChunkBytes + quad * 512, map, slab * 64, y0, y1, y2, y3, fb);
+            if (nch == 9 && slab == 0)
+                tma_gather4(base + 8 * kChunkBytes + quad * 512, map, 8 * 64, y0, y1, y2, y3, fb);
             ++cnt;
         }
     }
@@ -257,7 +249,8 @@ __device__ void producer(const TcArgs &p, const Sync &sy, uint8_t *ring, uint64_
 
 template <bool kBF16>
 __global__ void __launch_bounds__(kThreads, 1)
-    fwd_tc_kernel(const TcArgs p) {
+    fwd_tc_kernel(const TcArgs p, const __grid_constant__ CUtensorMap ori_map,
+                  const __grid_constant__ CUtensorMap cmp_map) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     Hdr *hd = reinterpret_cast<Hdr *>(smem);
@@ -268,7 +261,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kKStages; ++i) {
-            mbar_init(smem_u32(&hd->k_full[i]), kProdThreads);
+            mbar_init(smem_u32(&hd->k_full[i]), 1);
             mbar_init(smem_u32(&hd->k_empty[i]), 1);
         }
         for (int i = 0; i < 2; ++i) {
@@ -281,7 +274,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(smem_u32(&hd->p_full[i]), 1);
         }
         for (int i = 0; i < kVStages; ++i) {
-            mbar_init(smem_u32(&hd->v_full[i]), kProdThreads);
+            mbar_init(smem_u32(&hd->v_full[i]), 1);
             mbar_init(smem_u32(&hd->v_empty[i]), 1);
         }
         mbar_init(smem_u32(&hd->o_full), 1);
@@ -313,7 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t *kbuf = data;
         const uint32_t kstage = (uint32_t)qch * kChunkBytes;
         if (warp >= kProdWarp0 && warp < kProdWarp0 + 4) {
-            producer(p, sy, kbuf, hd->k_full, hd->k_empty, hd->rowbuf, kKStages, qch);
+            producer(p, sy, &ori_map, &cmp_map, kbuf, hd->k_full, hd->k_empty, hd->rowbuf, kKStages, qch);
         } else if (warp == kMmaWarp) {
             constexpr uint32_t idesc = idesc_f16(kBF16 ? 1u : 0u, 128, kBK, 0);
             uint32_t kc = 0, sc = 0, qc = 0;
@@ -326,7 +319,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int j = 0; j < it.ntiles; ++j, ++kc, ++sc) {
                     const int ks = kc % kKStages, sb = sc & 1;
                     if (!wait_warp(sy, smem_u32(&hd->k_full[ks]), (kc / kKStages) & 1)) goto done;
-                    fence_proxy_async_smem();  // cp.async (generic proxy) writes -> UMMA reads
                     if (!wait_warp(sy, smem_u32(&hd->s_free[sb]), ((sc >> 1) & 1) ^ 1)) goto done;
                     tc_fence_after();
                     if (lane == 0) {
@@ -466,7 +458,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t *msgs = data + kVStages * vch * kChunkBytes;
         const uint32_t vstage = (uint32_t)vch * kChunkBytes;
         if (warp >= kProdWarp0 && warp < kProdWarp0 + 4) {
-            producer(p, sy, vbuf, hd->v_full, hd->v_empty, hd->rowbuf, kVStages, vch);
+            producer(p, sy, &ori_map, &cmp_map, vbuf, hd->v_full, hd->v_empty, hd->rowbuf, kVStages, vch);
         } else if (warp == kMmaWarp) {
             const uint32_t nhalf = (uint32_t)p.Dv / 2;
             const uint32_t idesc = idesc_f16(kBF16 ? 1u : 0u, 128, nhalf, 1);
@@ -481,7 +473,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (!wait_warp(sy, smem_u32(&hd->p_full[ps]), (pc / kPStages) & 1, true)) goto done;
                     if (lane == 0) mbar_arrive_expect_tx(smem_u32(&hd->p_full[ps]), kMsgTx);  // next message
                     if (!wait_warp(sy, smem_u32(&hd->v_full[vs]), (vc / kVStages) & 1)) goto done;
-                    fence_proxy_async_smem();
                     uint8_t *msg = msgs + ps * kMsgBytes;
                     bool need = false;
                     for (int i = lane; i < 128; i += 32)
@@ -628,6 +619,38 @@ done:
     if (warp == kMmaWarp) tmem_dealloc(tmem, kTmemCols);
 }
 
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = [] {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            return reinterpret_cast<EncodeTiledFn>(ptr);
+        return static_cast<EncodeTiledFn>(nullptr);
+    }();
+    return fn;
+}
+
+// Row-gather tensor map over a paged pool viewed as [rows, D] (box: 64 columns x 1 row, 128-byte
+// swizzle).  Row `rows` (one past the end) lies outside the map and reads as zeros.
+int make_map(CUtensorMap *map, const void *base, int64_t rows, int D, bool bf16) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return SAS_ERR_CUDA;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || rows >= INT32_MAX) return SAS_ERR_INVALID_ARG;
+    cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)D * 2};
+    cuuint32_t box[2] = {64, 1};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                    const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? SAS_OK : SAS_ERR_CUDA;
+}
+
 } // namespace
 
 namespace sas_host {
@@ -668,6 +691,11 @@ int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const 
     p.ori_rows = a.ori_block_num * a.ori_block_size;
     p.cmp_rows = a.scenario >= 2 ? a.cmp_block_num * a.cmp_block_size : p.ori_rows;
     p.scale_log2 = a.softmax_scale * 1.4426950408889634f;
+    CUtensorMap ori_map, cmp_map;
+    int rc = make_map(&ori_map, ori_kv, p.ori_rows, a.head_dim, bf16);
+    if (rc) return rc;
+    rc = make_map(&cmp_map, a.scenario >= 2 ? cmp_kv : ori_kv, p.cmp_rows, a.head_dim, bf16);
+    if (rc) return rc;
     static bool attr_done[2] = {false, false};
     const int di = bf16 ? 0 : 1;
     if (!attr_done[di]) {
@@ -697,7 +725,8 @@ int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const 
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = bf16 ? cudaLaunchKernelEx(&cfg, fwd_tc_kernel<true>, p) : cudaLaunchKernelEx(&cfg, fwd_tc_kernel<false>, p);
+    cudaError_t e = bf16 ? cudaLaunchKernelEx(&cfg, fwd_tc_kernel<true>, p, ori_map, cmp_map)
+                         : cudaLaunchKernelEx(&cfg, fwd_tc_kernel<false>, p, ori_map, cmp_map);
     return check_cuda(e);
 }
 
