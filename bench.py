@@ -15,7 +15,8 @@ Printed by rank 0, one JSON line:
                it; time = max over ranks of the summed per-step CUDA-event times
   e2e          the same metric through the public API with host buffers: per
                step, the step's inputs copied from pinned host memory, the
-               call, and out + lse copied back to pinned host memory
+               call, and out + lse copied back to pinned host memory; steps
+               rotate over E2E_STREAMS CUDA streams so copies overlap compute
   roofline     HBM roofline of the attention kernel (algorithmic bytes per
                launch / its CUDA-event duration vs the measured copy peak)
   cpu_baseline the oracle CPU port on a bounded sample of the workload (rank 0, N=1)
@@ -40,6 +41,7 @@ sys.path.insert(0, REPO)
 import torch  # noqa: E402
 
 L2_FLUSH_BYTES = 256 << 20
+E2E_STREAMS = 3
 
 
 def parse():
@@ -323,41 +325,52 @@ def main():
     # ---- end to end through the public API with host buffers
     e2e = None
     if not args.no_e2e:
-        host = {}
+        # Every step copies its own inputs from pinned host memory, runs the public API call and
+        # reads its out + lse back into pinned host memory.  Steps rotate over E2E_STREAMS streams,
+        # so one step's copies overlap another's compute, as a serving loop would run them.
         pin = lambda x: x.cpu().pin_memory()  # noqa: E731
-        host["q"] = pin(q)
+        host = {"q": pin(q)}
         for k in ("cmp_sparse_indices", "cu_seqlens_q", "seqused_kv", "ori_block_table", "cmp_block_table", "sinks"):
             host[k] = pin(kw[k])
-        out_h = torch.empty((T, N1, Dv), dtype=q.dtype).pin_memory()
-        lse_h = torch.empty((T, N1), dtype=torch.float32).pin_memory()
+        streams = [torch.cuda.Stream(device=dev) for _ in range(E2E_STREAMS)]
+        outs_h = [(torch.empty((T, N1, Dv), dtype=q.dtype).pin_memory(),
+                   torch.empty((T, N1), dtype=torch.float32).pin_memory()) for _ in streams]
         h2d = sum(v.numel() * v.element_size() for v in host.values())
-        d2h = out_h.numel() * out_h.element_size() + lse_h.numel() * lse_h.element_size()
+        d2h = outs_h[0][0].numel() * outs_h[0][0].element_size() + outs_h[0][1].numel() * outs_h[0][1].element_size()
         base = {k: v for k, v in kw.items() if not isinstance(v, torch.Tensor) or k in ("ori_kv", "cmp_kv")}
 
-        def e2e_step():
-            d = {k: v.to(dev, non_blocking=True) for k, v in host.items()}
-            o, l_ = sparse_attn_sharedkv(d.pop("q"), return_softmax_lse=True, kernel=args.kernel,
-                                         max_seqlen_q=max_q, **d, **base)
-            out_h.copy_(o, non_blocking=True)
-            lse_h.copy_(l_, non_blocking=True)
+        def e2e_step(i):
+            st = streams[i % len(streams)]
+            out_h, lse_h = outs_h[i % len(streams)]
+            with torch.cuda.stream(st):
+                d = {k: v.to(dev, non_blocking=True) for k, v in host.items()}
+                o, l_ = sparse_attn_sharedkv(d.pop("q"), return_softmax_lse=True, kernel=args.kernel,
+                                             max_seqlen_q=max_q, **d, **base)
+                out_h.copy_(o, non_blocking=True)
+                lse_h.copy_(l_, non_blocking=True)
 
-        for _ in range(args.warmup):
-            e2e_step()
+        for i in range(args.warmup):
+            e2e_step(i)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(args.steps):
-            e2e_step()
-        e1.record()
+        cur = torch.cuda.current_stream()
+        e0.record(cur)
+        for st in streams:
+            st.wait_event(e0)
+        for i in range(args.steps):
+            e2e_step(i)
+        for st in streams:
+            cur.wait_stream(st)
+        e1.record(cur)
         torch.cuda.synchronize()
         te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
         if world > 1:
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
         e2e = {"value": tokens_all / (float(te.item()) / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-               "d2h_bytes_per_step": d2h}
+               "d2h_bytes_per_step": d2h, "streams": len(streams)}
 
     # ---- roofline of the attention kernel
     peaks = measured_peaks()

@@ -30,6 +30,8 @@ SAS_NOALLOC_SCRATCH_BYTES = 16 << 20
 SAS_DTYPE_BF16 = 0
 SAS_DTYPE_FP16 = 1
 
+SAS_FWD_FLAG_CU_SEQLENS = 0x1
+
 KERNELS = {"auto": 0, "simt": 1, "tc": 2}
 LAYOUT_Q = {"BSND": 0, "BSH": 1, "TND": 2}
 LAYOUT_KV = {"PA_ND": 0, "TND": 1}
@@ -75,7 +77,8 @@ class SasFwdArgs(ctypes.Structure):
         ("dtype", ctypes.c_int32),
         ("softmax_scale", ctypes.c_float),
         ("kernel", ctypes.c_int32),
-        ("reserved", ctypes.c_int32 * 6),
+        ("flags", ctypes.c_int32),
+        ("reserved", ctypes.c_int32 * 5),
     ]
 
 

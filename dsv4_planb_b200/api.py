@@ -119,8 +119,8 @@ def sparse_attn_sharedkv(
         q_flat = q
         cu = _i32(cu_seqlens_q, dev)
         B = cu.numel() - 1
-        q_prefix = cu[:-1]
-        act_q = (cu[1:] - cu[:-1]).contiguous()
+        q_prefix = cu  # with SAS_FWD_FLAG_CU_SEQLENS the kernels derive act_q = cu[b+1] - cu[b]
+        act_q = None
         if max_seqlen_q is None:
             cu_h = cu_seqlens_q.detach().to("cpu", torch.int64)
             max_seqlen_q = int((cu_h[1:] - cu_h[:-1]).max().item()) if B > 0 else 0
@@ -212,6 +212,7 @@ def sparse_attn_sharedkv(
     args.dtype = dtype_code
     args.softmax_scale = float(softmax_scale)
     args.kernel = _lib.KERNELS[kernel]
+    args.flags = _lib.SAS_FWD_FLAG_CU_SEQLENS if layout_q == "TND" else 0
 
     lib = _lib.load()
     nbytes = _lib.ctypes.c_size_t(0)

@@ -52,7 +52,8 @@ int validate_fwd(const SasFwdArgs &a) {
     if (a.scenario == 3 && a.topk < 0) return SAS_ERR_INVALID_ARG;
     if (a.scenario == 2 && a.max_cmp_len < 0) return SAS_ERR_INVALID_ARG;
     if (a.kernel < SAS_KERNEL_AUTO || a.kernel > SAS_KERNEL_TC) return SAS_ERR_INVALID_ARG;
-    for (int i = 0; i < 6; ++i)
+    if ((a.flags & ~SAS_FWD_FLAG_CU_SEQLENS) != 0) return SAS_ERR_INVALID_ARG;
+    for (int i = 0; i < 5; ++i)
         if (a.reserved[i] != 0) return SAS_ERR_INVALID_ARG;
     if (a.kernel == SAS_KERNEL_TC && !tc_supported(a)) return SAS_ERR_UNSUPPORTED;
     return SAS_OK;
@@ -121,7 +122,9 @@ int sas_workspace_size(const SasFwdArgs *args, size_t *bytes) {
 static int check_inputs(const SasFwdArgs &a, const void *ori_kv, const int32_t *ori_bt, const void *cmp_kv,
                         const int32_t *cmp_bt, const int32_t *idx, const int32_t *q_prefix, const int32_t *act_q,
                         const int32_t *act_kv) {
-    if (a.batch > 0 && (!q_prefix || !act_q || !act_kv || !ori_bt || !ori_kv)) return SAS_ERR_INVALID_ARG;
+    const bool need_act_q = (a.flags & SAS_FWD_FLAG_CU_SEQLENS) == 0;
+    if (a.batch > 0 && (!q_prefix || (need_act_q && !act_q) || !act_kv || !ori_bt || !ori_kv))
+        return SAS_ERR_INVALID_ARG;
     if (a.scenario >= 2 && (!cmp_kv || !cmp_bt)) return SAS_ERR_INVALID_ARG;
     if (a.scenario == 3 && a.topk > 0 && a.num_tokens > 0 && !idx) return SAS_ERR_INVALID_ARG;
     return SAS_OK;

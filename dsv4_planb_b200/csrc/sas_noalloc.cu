@@ -57,7 +57,8 @@ extern "C" int sas_forward_noalloc(const SasFwdArgs *args, const void *q, const 
     const SasFwdArgs &a = *args;
     int rc = sas_host::validate_fwd(a);
     if (rc) return rc;
-    if (a.batch > 0 && (!q_prefix || !act_q_len || !act_kv_len || !ori_block_table || !ori_kv))
+    if (a.batch > 0 && (!q_prefix || (!act_q_len && !(a.flags & SAS_FWD_FLAG_CU_SEQLENS)) || !act_kv_len ||
+                        !ori_block_table || !ori_kv))
         return SAS_ERR_INVALID_ARG;
     if (a.scenario >= 2 && (!cmp_kv || !cmp_block_table)) return SAS_ERR_INVALID_ARG;
     if (a.scenario == 3 && a.topk > 0 && a.num_tokens > 0 && !cmp_indices) return SAS_ERR_INVALID_ARG;

@@ -26,6 +26,7 @@ namespace {
 
 struct PrepArgs {
     int B, T, K, row_cap, scenario, ratio, win_left, win_right, max_q_len;
+    int cu;  // q_prefix is cu_seqlens_q [B + 1]; act_q is derived from it
     int cmp_block_num, cmp_block_size, cmp_table_len;
     const int32_t *cmp_bt, *idx, *q_prefix, *act_q, *act_kv;
     int32_t *tinfo, *rows;
@@ -96,7 +97,7 @@ __global__ void __launch_bounds__(kThreads) prep_kernel(PrepArgs p) {
     const int b = blockIdx.y;
     const int tid = threadIdx.x;
     if (b >= p.B) return;
-    const int aq = __ldg(p.act_q + b);
+    const int aq = p.cu ? __ldg(p.q_prefix + b + 1) - __ldg(p.q_prefix + b) : __ldg(p.act_q + b);
     if (s == 0 && tid == 0 && aq > p.max_q_len) sas::set_status(p.status, SAS_STATUS_BAD_TOKEN);
     if (s >= aq) return;
     const int akv = __ldg(p.act_kv + b);
@@ -186,6 +187,7 @@ namespace sas_host {
 // Zero the status word and the token records, then resolve every token.
 int launch_prep(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const int32_t *cmp_bt, const int32_t *idx,
                 const int32_t *q_prefix, const int32_t *act_q, const int32_t *act_kv, cudaStream_t s) {
+    const bool cu = (a.flags & SAS_FWD_FLAG_CU_SEQLENS) != 0;
     if (check_cuda(cudaMemsetAsync(ws + L.status, 0, sas::kAlign, s))) return SAS_ERR_CUDA;
     if (a.num_tokens > 0 &&
         check_cuda(cudaMemsetAsync(ws + L.token_info, 0, sizeof(int32_t) * sas::TI_INTS * (size_t)a.num_tokens, s)))
@@ -201,6 +203,7 @@ int launch_prep(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const in
     p.win_left = a.ori_win_left;
     p.win_right = a.ori_win_right;
     p.max_q_len = a.max_q_len;
+    p.cu = cu ? 1 : 0;
     p.cmp_block_num = a.cmp_block_num;
     p.cmp_block_size = a.cmp_block_size;
     p.cmp_table_len = a.cmp_table_len;

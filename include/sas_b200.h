@@ -72,8 +72,20 @@ typedef struct SasFwdArgs {
     int32_t dtype;          /* SasDtype of q, both pools and out */
     float softmax_scale;
     int32_t kernel;         /* SasKernel */
-    int32_t reserved[6];    /* must be 0 */
+    int32_t flags;          /* SAS_FWD_FLAG_* bits (0: the reference's q_prefix / act_q_len inputs) */
+    int32_t reserved[5];    /* must be 0 */
 } SasFwdArgs;
+
+/*
+ * SasFwdArgs.flags.
+ * SAS_FWD_FLAG_CU_SEQLENS: q_prefix points at cu_seqlens_q (batch + 1 entries,
+ *   the TND layout's cumulative lengths) and act_q_len may be NULL; the kernels
+ *   take act_q_len[b] = q_prefix[b + 1] - q_prefix[b].  A TND caller then needs
+ *   no device work of its own before the call (no act_q_len subtraction kernel).
+ *   No counterpart in the reference, whose API derives act_q_len with a tensor
+ *   op (api.py:208-240).
+ */
+#define SAS_FWD_FLAG_CU_SEQLENS 0x1
 
 /* Bytes of workspace sas_forward needs for `args` (256-byte aligned base). */
 int sas_workspace_size(const SasFwdArgs *args, size_t *bytes);
@@ -89,7 +101,8 @@ int sas_workspace_size(const SasFwdArgs *args, size_t *bytes);
  *   cmp_block_table [B, cmp_table_len] int32                (scenarios 2, 3; else NULL)
  *   cmp_indices  [T, 1, K] int32, -1 padded                  (scenario 3; else NULL)
  *   q_prefix     [B] int32: flat row of request b's first query token
- *   act_q_len    [B] int32
+ *                ([B + 1] cu_seqlens_q with SAS_FWD_FLAG_CU_SEQLENS)
+ *   act_q_len    [B] int32 (NULL allowed with SAS_FWD_FLAG_CU_SEQLENS)
  *   act_kv_len   [B] int32 (seqused_kv)
  *   sinks        [N1] fp32
  *   metadata     int32[1024] from sas_metadata / the reference scheduler, or

@@ -114,6 +114,18 @@ def test_forward_rejects_before_touching_the_device(lib):
     assert lib.sas_forward(None, *([None] * 13), None, 0, None) == _lib.SAS_ERR_INVALID_ARG
 
 
+def test_cu_seqlens_flag(lib):
+    # act_q_len may be NULL only with SAS_FWD_FLAG_CU_SEQLENS; unknown flag bits are rejected
+    a = good_args()
+    null = None
+    rc = lib.sas_forward(ctypes.byref(a), 1, 1, 1, 1, 1, 1, 1, null, 1, 1, null, 1, 1, 1, 1 << 30, null)
+    assert rc == _lib.SAS_ERR_INVALID_ARG
+    a.flags = 0x2
+    assert ws_size(lib, a)[0] == _lib.SAS_ERR_INVALID_ARG
+    a.flags = _lib.SAS_FWD_FLAG_CU_SEQLENS
+    assert ws_size(lib, a)[0] == _lib.SAS_OK
+
+
 def test_metadata_validation(lib):
     m = _lib.SasMetaArgs()
     m.num_heads_q, m.num_heads_kv, m.head_dim = 64, 1, 512
