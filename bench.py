@@ -18,7 +18,8 @@ Printed by rank 0, one JSON line:
                call, and out + lse copied back to pinned host memory; steps
                rotate over E2E_STREAMS CUDA streams so copies overlap compute
   roofline     HBM roofline of the attention kernel (algorithmic bytes per
-               launch / its CUDA-event duration vs the measured copy peak)
+               launch / its CUDA-event duration vs the measured copy peak), from
+               a second capture of the step with events around that kernel
   cpu_baseline the oracle CPU port on a bounded sample of the workload (rank 0, N=1)
 ``--impl reference`` times that CPU port alone (the reference is Python and
 its own kernel does not implement this scenario).
@@ -277,15 +278,22 @@ def main():
     k_start.record()  # creates the underlying cudaEvent_t handles
     k_stop.record()
     lib = _lib.load()
-    graph = torch.cuda.CUDAGraph()
     s = torch.cuda.Stream(device=dev)
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
         step()
     torch.cuda.current_stream().wait_stream(s)
+    # Two captures of the same step: `graph` (timed for `value`) holds only the op's own work;
+    # `graph_ev` also records the library's events around the attention kernel (its duration for
+    # the roofline).  The event nodes sit between the prep and the attention kernel and would
+    # otherwise serialise the programmatic launch that overlaps them.
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    graph_ev = torch.cuda.CUDAGraph()
     lib.sas_set_kernel_events(k_start.cuda_event, k_stop.cuda_event)
     try:
-        with torch.cuda.graph(graph):
+        with torch.cuda.graph(graph_ev):
             step()
     finally:
         lib.sas_set_kernel_events(None, None)
@@ -298,6 +306,8 @@ def main():
     for _ in range(args.warmup):
         flush.fill_(1.0)
         graph.replay()
+        flush.fill_(1.0)
+        graph_ev.replay()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -308,7 +318,10 @@ def main():
         starts[i].record()
         graph.replay()
         stops[i].record()
-        stops[i].synchronize()
+    for i in range(args.steps):
+        flush.fill_(float(i))
+        graph_ev.replay()
+        k_stop.synchronize()
         kernel_ms.append(k_start.elapsed_time(k_stop))
     torch.cuda.synchronize()
     clocks = sampler.stop()

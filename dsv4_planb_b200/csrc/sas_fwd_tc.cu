@@ -298,6 +298,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     cluster_sync();  // both CTAs' barriers are initialised before any remote arrive
     tc_fence_after();
+    // launched as a programmatic dependent of the prep kernel: everything above overlaps it; its
+    // token records and rows are complete and visible after this wait (a no-op otherwise)
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const uint32_t tmem = hd->tmem_base;
     Sync sy{hd, p.status, map_to_cta(smem_u32((const void *)&hd->abort), rank ^ 1u)};
 
@@ -718,13 +721,15 @@ int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const 
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = kSmemBytes;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // overlap the prep kernel's tail
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     cudaError_t e = bf16 ? cudaLaunchKernelEx(&cfg, fwd_tc_kernel<true>, p, ori_map, cmp_map)
                          : cudaLaunchKernelEx(&cfg, fwd_tc_kernel<false>, p, ori_map, cmp_map);
     return check_cuda(e);

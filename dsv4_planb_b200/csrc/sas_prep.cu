@@ -93,6 +93,9 @@ __global__ void __launch_bounds__(kThreads) prep_kernel(PrepArgs p) {
     __shared__ int warp_sums[kThreads / 32];
     __shared__ int s_stop;
     __shared__ int s_bad;
+    // the attention kernel is launched as a programmatic dependent of this one: let it start its
+    // prologue now (it waits for this grid's completion before reading the records)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int s = blockIdx.x;
     const int b = blockIdx.y;
     const int tid = threadIdx.x;
@@ -188,10 +191,10 @@ namespace sas_host {
 int launch_prep(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const int32_t *cmp_bt, const int32_t *idx,
                 const int32_t *q_prefix, const int32_t *act_q, const int32_t *act_kv, cudaStream_t s) {
     const bool cu = (a.flags & SAS_FWD_FLAG_CU_SEQLENS) != 0;
-    if (check_cuda(cudaMemsetAsync(ws + L.status, 0, sas::kAlign, s))) return SAS_ERR_CUDA;
-    if (a.num_tokens > 0 &&
-        check_cuda(cudaMemsetAsync(ws + L.token_info, 0, sizeof(int32_t) * sas::TI_INTS * (size_t)a.num_tokens, s)))
-        return SAS_ERR_CUDA;
+    // the status word and the token records are adjacent: one memset clears both
+    static_assert(sizeof(int32_t) * sas::TI_INTS % 16 == 0, "token record size");
+    const size_t clear = L.token_info + sizeof(int32_t) * sas::TI_INTS * (size_t)(a.num_tokens > 0 ? a.num_tokens : 0);
+    if (check_cuda(cudaMemsetAsync(ws + L.status, 0, clear - L.status, s))) return SAS_ERR_CUDA;
     if (a.batch == 0 || a.max_q_len == 0 || a.num_tokens == 0) return SAS_OK;
     PrepArgs p;
     p.B = a.batch;
