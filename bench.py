@@ -8,6 +8,8 @@ the BASELINE configuration ``c2`` (B = 64, seq U[8K, 32K]) per GPU, with
 synthetic seeded inputs (``dsv4_planb_b200.workloads``).  With N GPUs every
 rank runs its own c2 batch (seed 42 + rank): requests are independent and are
 sharded by batch with no collective on the data path ("weak" scaling).
+``--workload c5`` splits the 512 requests of c5 across the N ranks by cost
+instead (``dsv4_planb_b200.sharding``; "strong" scaling, total work fixed).
 
 Printed by rank 0, one JSON line:
   value        decode tokens/s of all ranks, inputs resident in HBM, each step
@@ -254,7 +256,19 @@ def main():
     from dsv4_planb_b200.roofline import algorithmic_figures
 
     _lib.load()
-    wl = W.config_workload(args.workload, seed=42 + rank, device=dev)
+    strong = args.workload == "c5"
+    if strong:
+        # c5 is the multi-GPU config: its 512 requests are split across the ranks by cost (LPT over
+        # window + compressed keys per token) and each rank builds only its shard's pools and tables.
+        from dsv4_planb_b200 import sharding as S
+
+        q_all, kv_all, n1, topk = W.config_lengths("c5", 42)
+        mine = S.partition_requests(S.request_costs(q_all, kv_all, topk), world)[rank]
+        wl = W.make_workload(name="c5[shard]", q_lens=[q_all[i] for i in mine], kv_lens=[kv_all[i] for i in mine],
+                             num_heads=n1, topk=topk, seed=42 + rank, device=dev)
+        total_tokens = sum(q_all)
+    else:
+        wl = W.config_workload(args.workload, seed=42 + rank, device=dev)
     figs = algorithmic_figures(wl, dev)
     kw = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in wl.api_kwargs().items()}
     q = wl.q
@@ -332,7 +346,7 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dist.barrier()
     max_total_ms = float(t.item())
-    tokens_all = T * world * args.steps
+    tokens_all = (total_tokens if strong else T * world) * args.steps
     value = tokens_all / (max_total_ms / 1e3)
 
     # ---- end to end through the public API with host buffers
@@ -417,13 +431,14 @@ def main():
         "warmup": args.warmup,
         "ms_per_step": max_total_ms / args.steps,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if strong else "weak",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic",
-        "config": {"workload": f"{args.workload}: {W.CONFIG_DESCRIPTIONS[args.workload]}", "global_batch": T * world,
+        "config": {"workload": f"{args.workload}: {W.CONFIG_DESCRIPTIONS[args.workload]}",
+                   "global_batch": total_tokens if strong else T * world,
                    "per_gpu_batch": T, "seq_len": "U[8K,32K]" if args.workload == "c2" else None,
-                   "parallelism": f"request-sharded x{world}", "l2": "flushed (256 MiB write) before every step",
+                   "parallelism": (f"LPT request shards x{world}" if strong else f"request-sharded x{world}"), "l2": "flushed (256 MiB write) before every step",
                    "timing": "CUDA graph replay per step, CUDA events, max over ranks"},
         "roofline": roofline,
         "cpu_baseline": cpu,
