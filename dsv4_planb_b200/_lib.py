@@ -31,6 +31,7 @@ SAS_DTYPE_BF16 = 0
 SAS_DTYPE_FP16 = 1
 
 SAS_FWD_FLAG_CU_SEQLENS = 0x1
+SAS_FWD_FLAG_TEST_STALL = 0x100
 
 KERNELS = {"auto": 0, "simt": 1, "tc": 2}
 LAYOUT_Q = {"BSND": 0, "BSH": 1, "TND": 2}

@@ -99,6 +99,7 @@ struct TcArgs {
     int T, N1, Dq, Dv, row_cap;
     int ori_block_num, ori_block_size, ori_table_len;
     int ori_rows, cmp_rows;  // rows of each pool: the out-of-range row index reads zeros
+    int test_stall;          // SAS_FWD_FLAG_TEST_STALL: withhold the first P-slot release
     float scale_log2;
 };
 
@@ -509,6 +510,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tc_fence_after();
                     fence_proxy_async_smem();
                     if (lane == 0) {
+                        const bool stall = p.test_stall && pc == 0;  // test hook, see SAS_FWD_FLAG_TEST_STALL
                         const uint32_t pa = smem_u32(msg);
                         const uint32_t vb = smem_u32(vbuf + (size_t)vs * vstage);
                         for (int hf = 0; hf < 2; ++hf) {
@@ -520,7 +522,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             }
                         }
                         tc_commit(smem_u32(&hd->v_empty[vs]));
-                        tc_commit_mc(smem_u32(&hd->p_empty[ps]), (uint16_t)1);
+                        if (!stall) tc_commit_mc(smem_u32(&hd->p_empty[ps]), (uint16_t)1);
                         if (last) tc_commit(smem_u32(&hd->o_full));
                     }
                     __syncwarp();
@@ -694,6 +696,7 @@ int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const 
     p.ori_rows = a.ori_block_num * a.ori_block_size;
     p.cmp_rows = a.scenario >= 2 ? a.cmp_block_num * a.cmp_block_size : p.ori_rows;
     p.scale_log2 = a.softmax_scale * 1.4426950408889634f;
+    p.test_stall = (a.flags & SAS_FWD_FLAG_TEST_STALL) ? 1 : 0;
     CUtensorMap ori_map, cmp_map;
     int rc = make_map(&ori_map, ori_kv, p.ori_rows, a.head_dim, bf16);
     if (rc) return rc;

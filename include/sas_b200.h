@@ -86,6 +86,14 @@ typedef struct SasFwdArgs {
  *   op (api.py:208-240).
  */
 #define SAS_FWD_FLAG_CU_SEQLENS 0x1
+/*
+ * SAS_FWD_FLAG_TEST_STALL: test hook for the failure path of the tensor-core
+ * kernel.  Its output CTAs withhold the release of their first P slot, so the
+ * score CTA's bounded wait for that slot runs out: the call completes, the
+ * status word reports SAS_STATUS_WAIT_TIMEOUT, and the context stays usable.
+ * Nothing faults, traps or spins without bound.
+ */
+#define SAS_FWD_FLAG_TEST_STALL 0x100
 
 /* Bytes of workspace sas_forward needs for `args` (256-byte aligned base). */
 int sas_workspace_size(const SasFwdArgs *args, size_t *bytes);
