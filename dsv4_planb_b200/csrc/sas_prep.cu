@@ -88,7 +88,7 @@ __device__ __forceinline__ int block_exscan(int v, int *total, int *warp_sums) {
 }
 
 template <int kPer>
-__global__ void __launch_bounds__(kThreads) prep_kernel(PrepArgs p) {
+__global__ void __launch_bounds__(kThreads, 1) prep_kernel(PrepArgs p) {
     __shared__ int32_t tab_s[kTableSmem];
     __shared__ int warp_sums[kThreads / 32];
     __shared__ int s_stop;
@@ -100,11 +100,21 @@ __global__ void __launch_bounds__(kThreads) prep_kernel(PrepArgs p) {
     const int b = blockIdx.y;
     const int tid = threadIdx.x;
     if (b >= p.B) return;
-    const int aq = p.cu ? __ldg(p.q_prefix + b + 1) - __ldg(p.q_prefix + b) : __ldg(p.act_q + b);
+    // Everything that depends on the request alone is loaded in one round trip (these reads miss
+    // L2 after a flush; the indices, which need the token row, form the second and last round).
+    const int q0 = __ldg(p.q_prefix + b);
+    const int aq = p.cu ? __ldg(p.q_prefix + b + 1) - q0 : __ldg(p.act_q + b);
+    const int akv = __ldg(p.act_kv + b);
+    const bool staged = p.scenario >= 2 && p.cmp_table_len <= kTableSmem;
+    int32_t tabv[kTableSmem / kThreads];
+#pragma unroll
+    for (int k = 0; k < kTableSmem / kThreads; ++k) {
+        const int i = tid + k * kThreads;
+        tabv[k] = staged && i < p.cmp_table_len ? __ldg(p.cmp_bt + (int64_t)b * p.cmp_table_len + i) : 0;
+    }
     if (s == 0 && tid == 0 && aq > p.max_q_len) sas::set_status(p.status, SAS_STATUS_BAD_TOKEN);
     if (s >= aq) return;
-    const int akv = __ldg(p.act_kv + b);
-    const int64_t t = (int64_t)__ldg(p.q_prefix + b) + s;
+    const int64_t t = (int64_t)q0 + s;
     if (t < 0 || t >= p.T) {
         if (tid == 0) sas::set_status(p.status, SAS_STATUS_BAD_TOKEN);
         return;
@@ -118,9 +128,13 @@ __global__ void __launch_bounds__(kThreads) prep_kernel(PrepArgs p) {
     int n_cmp = 0;
     int32_t *rows = p.rows + t * (int64_t)p.row_cap;
     if (p.scenario >= 2) {
-        const bool staged = p.cmp_table_len <= kTableSmem;
-        if (staged)
-            for (int i = tid; i < p.cmp_table_len; i += kThreads) tab_s[i] = __ldg(p.cmp_bt + (int64_t)b * p.cmp_table_len + i);
+        if (staged) {
+#pragma unroll
+            for (int k = 0; k < kTableSmem / kThreads; ++k) {
+                const int i = tid + k * kThreads;
+                if (i < p.cmp_table_len) tab_s[i] = tabv[k];
+            }
+        }
         if (tid == 0) {
             s_stop = 0x7fffffff;
             s_bad = 0;
