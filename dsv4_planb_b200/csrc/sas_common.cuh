@@ -25,6 +25,9 @@ enum TokenInfo : int {
 };
 
 constexpr size_t kAlign = 256;
+// Byte offset, inside the status block, of the tensor-core kernel's token counter (cleared with
+// the status word before every launch).
+constexpr size_t kTokenCounterOff = 64;
 inline size_t align_up(size_t x, size_t a = kAlign) { return (x + a - 1) / a * a; }
 
 // Workspace layout of sas_forward / sas_resolve_rows.

@@ -66,6 +66,12 @@ constexpr int kProdWarp0 = 4;
 constexpr int kProdThreads = 128;                    // warps 4-7
 constexpr int kMmaWarp = 8;
 
+// Token queue: the score CTA's producer warp 4 takes token ids from a global counter (the next one
+// fetched while the current one runs) and publishes them to every role of both CTAs through a
+// kTq-entry ring; an entry is reused once all kTqReaders consumer warps have read it.
+constexpr int kTq = 8;
+constexpr uint32_t kTqReaders = 17;  // every warp of the cluster but the writer: 8 in the score CTA, 9 in the output CTA
+
 constexpr int kTmemCols = 512;
 constexpr int kTmemS = 384;  // S buffers at columns 384 and 448 (Q uses columns [0, D_qk/2))
 
@@ -73,6 +79,8 @@ struct Hdr {
     uint64_t k_full[kKStages], k_empty[kKStages], s_full[2], s_free[2], q_full, p_empty[kPStages];
     uint64_t v_full[kVStages], v_empty[kVStages], p_full[kPStages], o_full, o_empty, rs_req, rs_done, pv_done,
         fin_ready;
+    uint64_t tq_full[kTq], tq_empty[kTq];  // token queue (tq_empty lives in the score CTA)
+    volatile int tq[kTq];
     uint32_t tmem_base;
     volatile int abort;
     int rs_stage;
@@ -81,9 +89,8 @@ struct Hdr {
     float fin_m[128];
     alignas(16) int32_t rowbuf[kKStages][kBK];  // physical rows of the tile gathered into each stage
 };
-static_assert(sizeof(Hdr) <= 2048, "header must fit in 2 KiB");
-
-constexpr int kDataOff = 2048;
+constexpr int kDataOff = 3072;  // 1 KiB aligned: the rings hold 128B-swizzled tiles
+static_assert(sizeof(Hdr) <= kDataOff, "header must fit before the data area");
 constexpr int kScoreSmem = kDataOff + kKStages * (kMaxDq / 64) * kChunkBytes;
 constexpr int kOutSmem = kDataOff + kVStages * (kMaxDv / 64) * kChunkBytes + kPStages * kMsgBytes;
 constexpr int kSmemBytes = (kScoreSmem > kOutSmem ? kScoreSmem : kOutSmem) + 1024;  // + alignment slack
@@ -100,6 +107,7 @@ struct TcArgs {
     int ori_block_num, ori_block_size, ori_table_len;
     int ori_rows, cmp_rows;  // rows of each pool: the out-of-range row index reads zeros
     int test_stall;          // SAS_FWD_FLAG_TEST_STALL: withhold the first P-slot release
+    int *counter;            // next token to hand out (zeroed with the status word before the launch)
     float scale_log2;
 };
 
@@ -166,6 +174,60 @@ __device__ __forceinline__ bool poll_warp(uint32_t bar, uint32_t parity) {
     return true;
 }
 
+// Token queue.  Cluster c's first token is c (every role takes it without the queue); later ones
+// come from the counter, offset by the cluster count, and pass through the queue: entry k >= 1
+// lives in slot (k - 1) % kTq.
+__device__ __forceinline__ int first_token(const TcArgs &p) {
+    return (int)cluster_id_x() < p.T ? (int)cluster_id_x() : -1;
+}
+
+// Reader side (every warp of the cluster but the writer; warp-uniform): the k-th token id of this
+// cluster, or -1 once the counter has passed the last token.  False on abort / timeout.
+__device__ __forceinline__ bool tq_read(const TcArgs &p, const Sync &sy, uint32_t rank, uint32_t k, int &t) {
+    if (k == 0) {
+        t = first_token(p);
+        return true;
+    }
+    const int s = (k - 1) % kTq;
+    if (!wait_warp(sy, smem_u32(&sy.h->tq_full[s]), ((k - 1) / kTq) & 1, true)) return false;
+    t = sy.h->tq[s];
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) {
+        const uint32_t e = smem_u32(&sy.h->tq_empty[s]);
+        if (rank == 0)
+            mbar_arrive(e);
+        else
+            mbar_arrive_remote(map_to_cta(e, 0));
+    }
+    return true;
+}
+
+// Writer side (score CTA, warp 4; warp-uniform).  `pend` (lane 0) holds the id taken while the
+// previous token's last tiles were being gathered (-1: none yet, take one now); taking it only
+// then keeps a cluster from holding a token it cannot start soon.
+__device__ __forceinline__ bool tq_publish(const TcArgs &p, const Sync &sy, uint32_t k, int &pend, int &t) {
+    if (k == 0) {
+        t = first_token(p);
+        return true;
+    }
+    const int s = (k - 1) % kTq;
+    const int lane = threadIdx.x & 31;
+    if (k - 1 >= (uint32_t)kTq && !wait_warp(sy, smem_u32(&sy.h->tq_empty[s]), (((k - 1) / kTq) - 1) & 1))
+        return false;
+    int v = 0;
+    if (lane == 0) {
+        if (pend < 0) pend = (int)ncluster_x() + atomicAdd(p.counter, 1);
+        v = pend < p.T ? pend : -1;
+        pend = -1;
+        sy.h->tq[s] = v;
+        st_cluster_u32(map_to_cta(smem_u32((const void *)&sy.h->tq[s]), 1), (uint32_t)v);
+        mbar_arrive(smem_u32(&sy.h->tq_full[s]));
+        mbar_arrive_remote(map_to_cta(smem_u32(&sy.h->tq_full[s]), 1));
+    }
+    t = __shfl_sync(0xffffffffu, v, 0);
+    return true;
+}
+
 // Row lookup of key k of tile j of an item, split in two so that the global
 // load (a block-table entry for window keys, a resolved row for compressed
 // keys) is issued one tile ahead and its latency hides behind the copies of
@@ -220,7 +282,13 @@ __device__ void producer(const TcArgs &p, const Sync &sy, const CUtensorMap *ori
     const int slab = pt >> 4, quad = pt & 15;
     const uint32_t stage_bytes = (uint32_t)nch * kChunkBytes;
     uint32_t cnt = 0;
-    for (int t = cluster_id_x(); t < p.T; t += ncluster_x()) {
+    const bool writer = cluster_rank() == 0 && (pt >> 5) == 0;
+    int pend = -1;
+    for (uint32_t k = 0;; ++k) {
+        int t = -1;
+        const bool got = writer ? tq_publish(p, sy, k, pend, t) : tq_read(p, sy, cluster_rank(), k, t);
+        if (!bar_red_and(2, kProdThreads, got)) return;
+        if (t < 0) break;
         const Item it = load_item(p, t);
         const int32_t *crow = p.rows + (int64_t)t * p.row_cap;
         int32_t fetched = pt < kBK && it.ntiles > 0 ? key_fetch(p, it, crow, 0, pt) : -1;
@@ -233,6 +301,8 @@ __device__ void producer(const TcArgs &p, const Sync &sy, const CUtensorMap *ori
             // all producer warps agree (abort) and see the tile's rows
             if (!bar_red_and(2, kProdThreads, ok)) return;
             if (pt < kBK && j + 1 < it.ntiles) fetched = key_fetch(p, it, crow, j + 1, pt);
+            if (writer && pt == 0 && j == (it.ntiles > 1 ? it.ntiles - 2 : 0))
+                pend = (int)ncluster_x() + atomicAdd(p.counter, 1);
             const bool win = j < it.nwt;
             const int32_t oob = win ? p.ori_rows : p.cmp_rows;
             const CUtensorMap *map = win ? ori_map : cmp_map;
@@ -284,6 +354,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(smem_u32(&hd->rs_done), 4);
         mbar_init(smem_u32(&hd->pv_done), 1);
         mbar_init(smem_u32(&hd->fin_ready), 1);
+        for (int i = 0; i < kTq; ++i) {
+            mbar_init(smem_u32(&hd->tq_full[i]), 1);
+            mbar_init(smem_u32(&hd->tq_empty[i]), kTqReaders);
+        }
         hd->abort = 0;
         hd->rs_stage = 0;
         // the output CTA expects the first message of each P stage (st.async complete_tx)
@@ -314,7 +388,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else if (warp == kMmaWarp) {
             constexpr uint32_t idesc = idesc_f16(kBF16 ? 1u : 0u, 128, kBK, 0);
             uint32_t kc = 0, sc = 0, qc = 0;
-            for (int t = cluster_id_x(); t < p.T; t += ncluster_x()) {
+            for (uint32_t k = 0;; ++k) {
+                int t;
+                if (!tq_read(p, sy, rank, k, t)) goto done;
+                if (t < 0) break;
                 const Item it = load_item(p, t);
                 if (it.ntiles == 0) continue;
                 if (!wait_warp(sy, smem_u32(&hd->q_full), qc & 1)) goto done;
@@ -345,7 +422,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t pfull0 = map_to_cta(smem_u32(&hd->p_full[0]), 1);  // the output CTA's barriers
             const float sink2 = h < p.N1 ? p.sinks[h] * 1.4426950408889634f : 0.f;
             uint32_t sc = 0, pc = 0;
-            for (int t = cluster_id_x(); t < p.T; t += ncluster_x()) {
+            for (uint32_t k = 0;; ++k) {
+                int t;
+                if (!tq_read(p, sy, rank, k, t)) goto done;
+                if (t < 0) break;
                 const Item it = load_item(p, t);
                 if (it.ntiles == 0) {
                     if (p.lse && h < p.N1) p.lse[(int64_t)t * p.N1 + h] = it.valid ? p.sinks[h] : 0.f;
@@ -467,7 +547,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t nhalf = (uint32_t)p.Dv / 2;
             const uint32_t idesc = idesc_f16(kBF16 ? 1u : 0u, 128, nhalf, 1);
             uint32_t vc = 0, pc = 0, oc = 0, pvc = 0, rsc = 0;
-            for (int t = cluster_id_x(); t < p.T; t += ncluster_x()) {
+            for (uint32_t k = 0;; ++k) {
+                int t;
+                if (!tq_read(p, sy, rank, k, t)) goto done;
+                if (t < 0) break;
                 const Item it = load_item(p, t);
                 if (it.ntiles == 0) continue;
                 if (!wait_warp(sy, smem_u32(&hd->o_empty), (oc & 1) ^ 1)) goto done;
@@ -533,7 +616,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
             uint32_t ofc = 0, rsc = 0, frc = 0;
             typedef typename std::conditional<kBF16, __nv_bfloat16, __half>::type OT;
-            for (int t = cluster_id_x(); t < p.T; t += ncluster_x()) {
+            for (uint32_t k = 0;; ++k) {
+                int t;
+                if (!tq_read(p, sy, rank, k, t)) goto done;
+                if (t < 0) break;
                 const Item it = load_item(p, t);
                 OT *orow = reinterpret_cast<OT *>(p.out) + ((int64_t)t * p.N1 + (h < p.N1 ? h : 0)) * p.Dv;
                 if (it.ntiles == 0) {
@@ -697,6 +783,7 @@ int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const 
     p.cmp_rows = a.scenario >= 2 ? a.cmp_block_num * a.cmp_block_size : p.ori_rows;
     p.scale_log2 = a.softmax_scale * 1.4426950408889634f;
     p.test_stall = (a.flags & SAS_FWD_FLAG_TEST_STALL) ? 1 : 0;
+    p.counter = reinterpret_cast<int *>(ws + L.status + sas::kTokenCounterOff);
     CUtensorMap ori_map, cmp_map;
     int rc = make_map(&ori_map, ori_kv, p.ori_rows, a.head_dim, bf16);
     if (rc) return rc;
