@@ -23,8 +23,10 @@ Printed by rank 0, one JSON line:
                launch / its CUDA-event duration vs the measured copy peak), from
                a second capture of the step with events around that kernel
   cpu_baseline the oracle CPU port on a bounded sample of the workload (rank 0, N=1)
-``--impl reference`` times that CPU port alone (the reference is Python and
-its own kernel does not implement this scenario).
+``--impl reference`` times that CPU port alone: the reference is Python over
+an NPU toolchain absent here, and its own TileLang kernel does not implement
+SCFA (it raises NotImplementedError), so its golden model, restated by the
+oracle, is the reference implementation of this path.
 """
 
 from __future__ import annotations

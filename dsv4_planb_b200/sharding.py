@@ -1,7 +1,7 @@
 """Request sharding of one decode batch across the GPUs of a node.
 
-Requests are independent (SURVEY: the path has no exchange step), so each
-rank runs ``sparse_attn_sharedkv`` on its own subset of requests over its own
+Requests are independent (no step of the path exchanges data between
+requests), so each rank runs ``sparse_attn_sharedkv`` on its own subset of requests over its own
 slice of the paged pools, with block ids remapped to that slice.  NCCL is used
 only to bring outputs back together for verification.
 

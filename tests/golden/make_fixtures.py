@@ -292,7 +292,7 @@ def make_baselines(G):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference-dir", default="/root/reference")
+    ap.add_argument("--reference-dir", required=True, help="checkout of the reference project")
     ap.add_argument("--only", default="")
     args = ap.parse_args()
     torch.set_num_threads(max(1, os.cpu_count() or 1))
