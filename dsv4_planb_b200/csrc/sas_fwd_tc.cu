@@ -267,8 +267,11 @@ __device__ __forceinline__ int32_t key_row(const TcArgs &p, const Item &it, int 
 // tile::gather4 (4 rows x 128 bytes per copy), in the UMMA K-major SW128
 // layout the tensor map's swizzle produces: row r of slab c at c * 8 KiB +
 // r * 128, 16-byte granule g at (g ^ r % 8) * 16.  Thread pt issues the copy
-// of slab pt / 16, rows 4 (pt % 16) .. +3 (and, with nch = 9, threads 0-15 the
-// ninth slab's); masked rows point one past the pool and read zeros.  Thread 0
+// of slab pt / 16, rows 4 (pt % 16) .. +3; with nch = 9, lanes 0-3 of each
+// warp also take four quads of the ninth slab, so every warp issues 36 copies.
+// A warp's copies enter the TMA unit one after another: with the ninth slab on
+// warp 4 alone (48 copies against 32) the c2 kernel took 112 us, balanced 104.
+// Masked rows point one past the pool and read zeros.  Thread 0
 // arms the stage's full barrier with the tile's byte count before the
 // producer barrier, so every copy's complete_tx lands on an armed phase.  The
 // row lookups of the next tile load while this tile's copies issue.
@@ -279,7 +282,7 @@ __device__ __forceinline__ int32_t key_row(const TcArgs &p, const Item &it, int 
 __device__ void producer(const TcArgs &p, const Sync &sy, const CUtensorMap *ori_map, const CUtensorMap *cmp_map,
                          uint8_t *ring, uint64_t *full, uint64_t *empty, int32_t (*rowbuf)[kBK], int stages, int nch) {
     const int pt = threadIdx.x - kProdWarp0 * 32;
-    const int slab = pt >> 4, quad = pt & 15;
+    const int slab = pt >> 4, quad = pt & 15, lane = pt & 31;
     const uint32_t stage_bytes = (uint32_t)nch * kChunkBytes;
     uint32_t cnt = 0;
     const bool writer = cluster_rank() == 0 && (pt >> 5) == 0;
@@ -311,8 +314,12 @@ __device__ void producer(const TcArgs &p, const Sync &sy, const CUtensorMap *ori
             const int y0 = r4.x >= 0 ? r4.x : oob, y1 = r4.y >= 0 ? r4.y : oob, y2 = r4.z >= 0 ? r4.z : oob,
                       y3 = r4.w >= 0 ? r4.w : oob;
             tma_gather4(base + slab * kChunkBytes + quad * 512, map, slab * 64, y0, y1, y2, y3, fb);
-            if (nch == 9 && slab == 0)
-                tma_gather4(base + 8 * kChunkBytes + quad * 512, map, 8 * 64, y0, y1, y2, y3, fb);
+            if (nch == 9 && lane < 4) {  // the ninth slab: quads 4w .. 4w+3 from warp w
+                const int q9 = 4 * (pt >> 5) + lane;
+                const int4 s4 = reinterpret_cast<const int4 *>(rowbuf[st])[q9];
+                tma_gather4(base + 8 * kChunkBytes + q9 * 512, map, 8 * 64, s4.x >= 0 ? s4.x : oob,
+                            s4.y >= 0 ? s4.y : oob, s4.z >= 0 ? s4.z : oob, s4.w >= 0 ? s4.w : oob, fb);
+            }
             ++cnt;
         }
     }
