@@ -474,13 +474,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                     __syncwarp();
                     if (lane == 0) mbar_arrive(smem_u32(&hd->s_free[sb]));
                     const int nvalid = j < it.nwt ? min(kBK, it.n_win - j * kBK) : min(kBK, it.n_cmp - (j - it.nwt) * kBK);
-                    float mx = -INFINITY;
+                    // four independent max / sum chains: one warp per SM sub-partition runs this, so
+                    // the latency of a single 64-long dependent chain would not be hidden
+                    float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+                    if (nvalid == kBK) {
 #pragma unroll
-                    for (int k = 0; k < kBK; ++k) {
-                        const float x = k < nvalid ? __uint_as_float(sr[k]) * p.scale_log2 : -INFINITY;
-                        sr[k] = __float_as_uint(x);
-                        mx = fmaxf(mx, x);
+                        for (int k = 0; k < kBK; ++k) {
+                            const float x = __uint_as_float(sr[k]) * p.scale_log2;
+                            sr[k] = __float_as_uint(x);
+                            mx4[k & 3] = fmaxf(mx4[k & 3], x);
+                        }
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < kBK; ++k) {
+                            const float x = k < nvalid ? __uint_as_float(sr[k]) * p.scale_log2 : -INFINITY;
+                            sr[k] = __float_as_uint(x);
+                            mx4[k & 3] = fmaxf(mx4[k & 3], x);
+                        }
                     }
+                    const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
                     float alpha = 1.f;
                     bool need = false;
                     if (j == 0) {
@@ -497,11 +509,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                         need = true;
                     }
                     uint32_t pk[32];
-                    float sum = 0.f, sumr = 0.f;
+                    float sum4[4] = {0.f, 0.f, 0.f, 0.f}, sumr4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                     for (int k = 0; k < kBK; k += 2) {
-                        const float p0 = exp2f(__uint_as_float(sr[k]) - m);
-                        const float p1 = exp2f(__uint_as_float(sr[k + 1]) - m);
+                        const float p0 = ex2_approx(__uint_as_float(sr[k]) - m);
+                        const float p1 = ex2_approx(__uint_as_float(sr[k + 1]) - m);
+                        float &sum = sum4[(k >> 1) & 3], &sumr = sumr4[(k >> 1) & 3];
                         sum += p0 + p1;
                         float2 pr;
                         if constexpr (kBF16) {
@@ -515,8 +528,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                         sumr += pr.x + pr.y;
                     }
-                    l += sum;
-                    lr += sumr;
+                    l += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
+                    lr += (sumr4[0] + sumr4[1]) + (sumr4[2] + sumr4[3]);
                     (void)need;
                     const bool last = j == it.ntiles - 1;
                     const int ps = pc % kPStages;

@@ -57,6 +57,14 @@ __device__ __forceinline__ bool mbar_try_cluster(uint32_t bar, uint32_t parity) 
     return ok != 0;
 }
 
+// 2^x with the MUFU approximation (PTX ex2.approx.ftz.f32: ~2 ulp, subnormal results flushed
+// to zero).  Used for softmax weights, which are rounded to bf16/fp16 afterwards.
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // ---- cluster ----------------------------------------------------------------
 __device__ __forceinline__ uint32_t cluster_rank() {
     uint32_t r;
