@@ -57,6 +57,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
     ap.add_argument("--kernel", default="auto", choices=["auto", "simt", "tc"])
+    ap.add_argument("--batch", type=int, default=None,
+                    help="request count of c2 / c3 (default 64 / 32): small-batch decode measurements")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
@@ -205,7 +207,7 @@ def run_reference(args, rank, world):
     from dsv4_planb_b200 import workloads as W
 
     torch.set_num_threads(os.cpu_count() or 1)
-    wl = W.config_workload(args.workload, device="cpu", index_method="keys")
+    wl = W.config_workload(args.workload, device="cpu", index_method="keys", batch=args.batch)
     times = []
     tokens = 0
     per_step_budget = 4.0
@@ -230,7 +232,9 @@ def run_reference(args, rank, world):
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": W.CONFIG_DESCRIPTIONS[args.workload], "global_batch": wl.num_tokens, "seq_len": None,
+        "config": {"workload": W.CONFIG_DESCRIPTIONS[args.workload]
+                               + (f" (batch overridden: {args.batch} requests)" if args.batch else ""),
+                   "global_batch": wl.num_tokens, "seq_len": None,
                    "parallelism": "cpu"},
         "cpu_baseline": {**times[-1], "value": value},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -270,7 +274,7 @@ def main():
                              num_heads=n1, topk=topk, seed=42 + rank, device=dev)
         total_tokens = sum(q_all)
     else:
-        wl = W.config_workload(args.workload, seed=42 + rank, device=dev)
+        wl = W.config_workload(args.workload, seed=42 + rank, device=dev, batch=args.batch)
     figs = algorithmic_figures(wl, dev)
     kw = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in wl.api_kwargs().items()}
     q = wl.q
@@ -409,7 +413,8 @@ def main():
     kname = "sas_fwd_tc" if args.kernel != "simt" and _tc_used(wl) else "fwd_simt_kernel"
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": achieved / peaks["hbm_gbs"] if achieved else None,
-                "traffic": committed_traffic(args.workload, kname), "peak_source": peaks["source"],
+                "traffic": None if args.batch else committed_traffic(args.workload, kname),
+                "peak_source": peaks["source"],
                 "kernel": kname, "kernel_ms": k_avg_ms, "bytes_per_launch": figs["bytes"],
                 "flops_per_launch": figs["flops"], "tflops": tflops,
                 "tensor_frac_of_burst": tflops / peaks["bf16_tflops"] if tflops else None}
@@ -437,7 +442,8 @@ def main():
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic",
-        "config": {"workload": f"{args.workload}: {W.CONFIG_DESCRIPTIONS[args.workload]}",
+        "config": {"workload": f"{args.workload}: {W.CONFIG_DESCRIPTIONS[args.workload]}"
+                               + (f" (batch overridden: {args.batch} requests)" if args.batch else ""),
                    "global_batch": total_tokens if strong else T * world,
                    "per_gpu_batch": T, "seq_len": "U[8K,32K]" if args.workload == "c2" else None,
                    "parallelism": (f"LPT request shards x{world}" if strong else f"request-sharded x{world}"), "l2": "flushed (256 MiB write) before every step",
@@ -445,7 +451,7 @@ def main():
         "roofline": roofline,
         "cpu_baseline": cpu,
         "e2e": e2e,
-        "gpu_launches": 2 * args.steps,
+        "gpu_launches": _kernels_per_call(wl, args.kernel) * args.steps,
         "clocks": clocks,
         "algorithmic": {"kv_bytes": figs["kv_bytes"], "keys": figs["keys"]},
     }
@@ -465,6 +471,24 @@ def _tc_used(wl) -> bool:
     a.dtype, a.softmax_scale, a.kernel = 0, 1.0, 2
     n = _lib.ctypes.c_size_t()
     return _lib.load().sas_workspace_size(_lib.ctypes.byref(a), _lib.ctypes.byref(n)) == 0
+
+
+def _kernels_per_call(wl, kernel: str) -> int:
+    """Kernels one sas_forward call on this workload launches (sas_forward_kernel_count)."""
+    from dsv4_planb_b200 import _lib
+
+    a = _lib.SasFwdArgs()
+    a.batch, a.num_tokens, a.max_q_len = len(wl.q_lens), wl.num_tokens, max(wl.q_lens)
+    a.num_heads, a.num_kv_heads, a.head_dim, a.v_head_dim = wl.q.shape[1], 1, wl.q.shape[2], wl.v_head_dim
+    a.ori_block_num, a.ori_block_size, a.ori_table_len = wl.ori_kv.shape[0], wl.ori_kv.shape[1], wl.ori_block_table.shape[1]
+    a.cmp_block_num, a.cmp_block_size, a.cmp_table_len = wl.cmp_kv.shape[0], wl.cmp_kv.shape[1], wl.cmp_block_table.shape[1]
+    a.topk, a.cmp_ratio, a.scenario = wl.topk, wl.cmp_ratio, 3
+    a.ori_win_left, a.ori_win_right, a.ori_mask_mode, a.cmp_mask_mode = 127, 0, 4, 3
+    a.dtype, a.softmax_scale, a.kernel = 0, wl.softmax_scale, _lib.KERNELS[kernel]
+    a.flags = _lib.SAS_FWD_FLAG_CU_SEQLENS
+    n = _lib.ctypes.c_int32(0)
+    _lib.check(_lib.load().sas_forward_kernel_count(_lib.ctypes.byref(a), _lib.ctypes.byref(n)), "kernel count")
+    return n.value
 
 
 if __name__ == "__main__":

@@ -40,6 +40,7 @@ LAYOUT_KV = {"PA_ND": 0, "TND": 1}
 # Every symbol include/sas_b200.h declares.
 EXPORTS = (
     "sas_workspace_size",
+    "sas_forward_kernel_count",
     "sas_forward",
     "sas_forward_noalloc",
     "sas_resolve_rows",
@@ -117,6 +118,7 @@ _SZ = ctypes.c_size_t
 
 _SIGNATURES = {
     "sas_workspace_size": (ctypes.c_int, [ctypes.POINTER(SasFwdArgs), ctypes.POINTER(_SZ)]),
+    "sas_forward_kernel_count": (ctypes.c_int, [ctypes.POINTER(SasFwdArgs), ctypes.POINTER(ctypes.c_int32)]),
     "sas_forward": (ctypes.c_int, [ctypes.POINTER(SasFwdArgs)] + [_P] * 13 + [_P, _SZ, _P]),
     "sas_forward_noalloc": (ctypes.c_int, [ctypes.POINTER(SasFwdArgs)] + [_P] * 13 + [_P]),
     "sas_resolve_rows": (ctypes.c_int, [ctypes.POINTER(SasFwdArgs)] + [_P] * 8 + [_P, _SZ, _P]),

@@ -21,6 +21,7 @@ int launch_fwd_simt(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, cons
                     cudaStream_t s);
 bool tc_supported(const SasFwdArgs &a);
 size_t tc_workspace(const SasFwdArgs &a);
+int tc_kernel_count(const SasFwdArgs &a);
 int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const void *q, const void *ori_kv,
                   const int32_t *ori_bt, const void *cmp_kv, const float *sinks, void *out, float *lse,
                   cudaStream_t s);
@@ -116,6 +117,18 @@ int sas_workspace_size(const SasFwdArgs *args, size_t *bytes) {
     int rc = validate_fwd(*args);
     if (rc) return rc;
     *bytes = fwd_layout(*args).total;
+    return SAS_OK;
+}
+
+int sas_forward_kernel_count(const SasFwdArgs *args, int32_t *count) {
+    if (!args || !count) return SAS_ERR_INVALID_ARG;
+    const SasFwdArgs &a = *args;
+    int rc = validate_fwd(a);
+    if (rc) return rc;
+    const int prep = (a.batch == 0 || a.max_q_len == 0 || a.num_tokens == 0) ? 0 : 1;
+    int attn = 0;
+    if (a.num_tokens > 0) attn = use_tc(a) ? tc_kernel_count(a) : (a.num_heads > 0 ? 1 : 0);
+    *count = prep + attn;
     return SAS_OK;
 }
 

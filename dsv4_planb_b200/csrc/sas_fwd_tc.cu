@@ -57,11 +57,19 @@ constexpr uint64_t kTimeoutNs = 4000000000ull;
 
 // P message: bf16 P [128 heads][64 keys] (SW128 K-major) + per-head floats.
 constexpr int kPBytes = 128 * kBK * 2;  // 16 KiB
-constexpr int kMsgAlpha = kPBytes;
-constexpr int kMsgL = kMsgAlpha + 512;
-constexpr int kMsgM = kMsgL + 512;
+// Per-head statistics after P: alpha (rescale factor of O), lr (sum of the rounded P), m (running
+// max) and, for pieces of split tokens, l (sum of the unrounded P, for the piece's LSE).  Whole
+// tokens: three float arrays [128] (alpha, lr, m), so the output CTA's per-tile scan of alpha reads
+// consecutive words.  Pieces: 16 bytes per head {alpha, lr, m, l}, one st.async each.
+constexpr int kMsgStats = kPBytes;
+constexpr int kMsgAlpha = 0, kMsgL = 1, kMsgM = 2, kMsgLs = 3;  // field index (array, or float in a head's 16 bytes)
+template <bool kSplit> __device__ __forceinline__ int stat_index(int h, int field) {
+    return kSplit ? 4 * h + field : 128 * field + h;
+}
 constexpr int kMsgBytes = 18 * 1024;
-constexpr uint32_t kMsgTx = 128 * (8 * 16 + 3 * 4);  // bytes st.async delivers per message
+static_assert(kMsgStats + 128 * 16 <= kMsgBytes, "P message layout");
+// bytes st.async delivers per message: P plus three or four statistics per head
+template <bool kSplit> constexpr uint32_t msg_tx() { return 128 * (8 * 16 + (kSplit ? 16 : 12)); }
 constexpr int kProdWarp0 = 4;
 constexpr int kProdThreads = 128;                    // warps 4-7
 constexpr int kMmaWarp = 8;
@@ -72,6 +80,7 @@ constexpr int kMmaWarp = 8;
 constexpr int kTq = 8;
 constexpr uint32_t kTqReaders = 17;  // every warp of the cluster but the writer: 8 in the score CTA, 9 in the output CTA
 
+constexpr int kMaxPieces = 64;  // pieces per token in split KV
 constexpr int kTmemCols = 512;
 constexpr int kTmemS = 384;  // S buffers at columns 384 and 448 (Q uses columns [0, D_qk/2))
 
@@ -87,6 +96,8 @@ struct Hdr {
     int pad;
     float fin_l[128];
     float fin_m[128];
+    float fin_ls[128];
+
     alignas(16) int32_t rowbuf[kKStages][kBK];  // physical rows of the tile gathered into each stage
 };
 constexpr int kDataOff = 3072;  // 1 KiB aligned: the rings hold 128B-swizzled tiles
@@ -107,12 +118,21 @@ struct TcArgs {
     int ori_block_num, ori_block_size, ori_table_len;
     int ori_rows, cmp_rows;  // rows of each pool: the out-of-range row index reads zeros
     int test_stall;          // SAS_FWD_FLAG_TEST_STALL: withhold the first P-slot release
-    int *counter;            // next token to hand out (zeroed with the status word before the launch)
+    int *counter;            // next unit to hand out (zeroed with the status word before the launch)
     float scale_log2;
+    // Split KV: token t's tiles are cut into pieces of M tiles; unit u is piece u / T of token
+    // u % T (U = T * P units).  P = 1: one unit per token.  Every piece of a token cut into
+    // np > 1 pieces leaves o = O / lr (bf16) and (m, l, lr) in slot (t, piece); combine_kernel
+    // merges them.
+    int P, M, U;
+    uint16_t *part_o;        // [T][P][N1][Dv]
+    float *part_s;           // [T][P][N1][4]: m, l, lr, unused
 };
 
 struct Item {
     int valid, b, left, n_win, n_cmp, nwt, ntiles;
+    int t, piece, np, j0, j1;  // the unit: tiles [j0, j1) of token t, piece `piece` of np
+    bool skip;                 // a piece past the token's last tile: nothing to do
 };
 
 __device__ __forceinline__ Item load_item(const TcArgs &p, int t) {
@@ -125,6 +145,30 @@ __device__ __forceinline__ Item load_item(const TcArgs &p, int t) {
     it.n_cmp = ti[sas::TI_NCMP];
     it.nwt = (it.n_win + kBK - 1) / kBK;
     it.ntiles = it.valid ? it.nwt + (it.n_cmp + kBK - 1) / kBK : 0;
+    return it;
+}
+
+// kSplit = false (P = 1): unit u is token u, all of its tiles; the loops compile as for whole tokens.
+template <bool kSplit>
+__device__ __forceinline__ Item load_unit(const TcArgs &p, int u) {
+    if constexpr (!kSplit) {
+        Item it = load_item(p, u);
+        it.t = u;
+        it.piece = 0;
+        it.np = 1;
+        it.skip = false;
+        it.j0 = 0;
+        it.j1 = it.ntiles;
+        return it;
+    }
+    const int piece = u / p.T, t = u - piece * p.T;
+    Item it = load_item(p, t);
+    it.t = t;
+    it.piece = piece;
+    it.np = p.P > 1 && it.ntiles > p.M ? min((it.ntiles + p.M - 1) / p.M, p.P) : 1;
+    it.skip = piece >= it.np;
+    it.j0 = it.np > 1 ? piece * p.M : 0;
+    it.j1 = it.np > 1 && piece < it.np - 1 ? it.j0 + p.M : it.ntiles;  // the last piece takes the rest
     return it;
 }
 
@@ -178,7 +222,7 @@ __device__ __forceinline__ bool poll_warp(uint32_t bar, uint32_t parity) {
 // come from the counter, offset by the cluster count, and pass through the queue: entry k >= 1
 // lives in slot (k - 1) % kTq.
 __device__ __forceinline__ int first_token(const TcArgs &p) {
-    return (int)cluster_id_x() < p.T ? (int)cluster_id_x() : -1;
+    return (int)cluster_id_x() < p.U ? (int)cluster_id_x() : -1;
 }
 
 // Reader side (every warp of the cluster but the writer; warp-uniform): the k-th token id of this
@@ -217,7 +261,7 @@ __device__ __forceinline__ bool tq_publish(const TcArgs &p, const Sync &sy, uint
     int v = 0;
     if (lane == 0) {
         if (pend < 0) pend = (int)ncluster_x() + atomicAdd(p.counter, 1);
-        v = pend < p.T ? pend : -1;
+        v = pend < p.U ? pend : -1;
         pend = -1;
         sy.h->tq[s] = v;
         st_cluster_u32(map_to_cta(smem_u32((const void *)&sy.h->tq[s]), 1), (uint32_t)v);
@@ -279,6 +323,7 @@ __device__ __forceinline__ int32_t key_row(const TcArgs &p, const Item &it, int 
 // Measured on the c2 decode batch: the score CTA's gather bounds the kernel.
 // Per SM, TMA gather4 sustains more random-row ingest than 16-byte cp.async
 // (~40 vs ~30 GB/s in isolation; 113 vs 121 us for the kernel).
+template <bool kSplit>
 __device__ void producer(const TcArgs &p, const Sync &sy, const CUtensorMap *ori_map, const CUtensorMap *cmp_map,
                          uint8_t *ring, uint64_t *full, uint64_t *empty, int32_t (*rowbuf)[kBK], int stages, int nch) {
     const int pt = threadIdx.x - kProdWarp0 * 32;
@@ -292,10 +337,11 @@ __device__ void producer(const TcArgs &p, const Sync &sy, const CUtensorMap *ori
         const bool got = writer ? tq_publish(p, sy, k, pend, t) : tq_read(p, sy, cluster_rank(), k, t);
         if (!bar_red_and(2, kProdThreads, got)) return;
         if (t < 0) break;
-        const Item it = load_item(p, t);
-        const int32_t *crow = p.rows + (int64_t)t * p.row_cap;
-        int32_t fetched = pt < kBK && it.ntiles > 0 ? key_fetch(p, it, crow, 0, pt) : -1;
-        for (int j = 0; j < it.ntiles; ++j) {
+        const Item it = load_unit<kSplit>(p, t);
+        if (it.skip) continue;
+        const int32_t *crow = p.rows + (int64_t)it.t * p.row_cap;
+        int32_t fetched = pt < kBK && it.j1 > it.j0 ? key_fetch(p, it, crow, it.j0, pt) : -1;
+        for (int j = it.j0; j < it.j1; ++j) {
             const int st = cnt % stages;
             const uint32_t fb = smem_u32(&full[st]);
             const bool ok = wait_warp(sy, smem_u32(&empty[st]), ((cnt / stages) & 1) ^ 1);
@@ -303,8 +349,8 @@ __device__ void producer(const TcArgs &p, const Sync &sy, const CUtensorMap *ori
             if (ok && pt == 0) mbar_arrive_expect_tx(fb, stage_bytes);
             // all producer warps agree (abort) and see the tile's rows
             if (!bar_red_and(2, kProdThreads, ok)) return;
-            if (pt < kBK && j + 1 < it.ntiles) fetched = key_fetch(p, it, crow, j + 1, pt);
-            if (writer && pt == 0 && j == (it.ntiles > 1 ? it.ntiles - 2 : 0))
+            if (pt < kBK && j + 1 < it.j1) fetched = key_fetch(p, it, crow, j + 1, pt);
+            if (writer && pt == 0 && j == (it.j1 - it.j0 > 1 ? it.j1 - 2 : it.j0))
                 pend = (int)ncluster_x() + atomicAdd(p.counter, 1);
             const bool win = j < it.nwt;
             const int32_t oob = win ? p.ori_rows : p.cmp_rows;
@@ -325,7 +371,55 @@ __device__ void producer(const TcArgs &p, const Sync &sy, const CUtensorMap *ori
     }
 }
 
-template <bool kBF16>
+// 32 consecutive outputs of one row, rounded to the output type, as four 16-byte stores.
+template <bool kBF16, typename OT>
+__device__ __forceinline__ void store_row32(OT *dst, const float (&x)[32]) {
+    uint32_t w[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+        if constexpr (kBF16) {
+            __nv_bfloat162 v = __floats2bfloat162_rn(x[2 * k], x[2 * k + 1]);
+            w[k] = *reinterpret_cast<uint32_t *>(&v);
+        } else {
+            __half2 v = __floats2half2_rn(x[2 * k], x[2 * k + 1]);
+            w[k] = *reinterpret_cast<uint32_t *>(&v);
+        }
+    }
+    uint4 *d = reinterpret_cast<uint4 *>(dst);
+#pragma unroll
+    for (int v = 0; v < 4; ++v) d[v] = make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
+}
+
+// Epilogue of one piece of a split token (output CTA warps 0-3, thread h = head; O of the piece in
+// TMEM at `trow`, its m, l and lr in fin_*): publish o = O / lr as bf16 and (m, l, lr) in the
+// token's slot of this piece.  combine_kernel merges the pieces after the launch.
+__device__ void write_partial(const TcArgs &p, const Hdr *hd, const Item &it, uint32_t trow) {
+    const int h = threadIdx.x;
+    const int nh = p.N1, hh = h < nh ? h : 0;  // every lane stays for the warp-wide TMEM loads
+    const int64_t sl = (int64_t)it.t * p.P + it.piece;
+    const float inv = 1.f / hd->fin_l[h];
+    uint16_t *po = p.part_o + (sl * nh + hh) * p.Dv;
+    for (int c = 0; c < p.Dv / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(trow + c * 32, r);
+        tc_wait_ld();
+        if (h < nh) {
+            float x[32];
+#pragma unroll
+            for (int k = 0; k < 32; ++k) x[k] = __uint_as_float(r[k]) * inv;
+            store_row32<true>(reinterpret_cast<__nv_bfloat16 *>(po + c * 32), x);
+        }
+    }
+    if (h < nh) {
+        float *ps = p.part_s + (sl * nh + h) * 4;
+        ps[0] = hd->fin_m[h];
+        ps[1] = hd->fin_ls[h];
+        ps[2] = hd->fin_l[h];
+        ps[3] = 0.f;
+    }
+}
+
+template <bool kBF16, bool kSplit>
 __global__ void __launch_bounds__(kThreads, 1)
     fwd_tc_kernel(const TcArgs p, const __grid_constant__ CUtensorMap ori_map,
                   const __grid_constant__ CUtensorMap cmp_map) {
@@ -369,7 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         hd->rs_stage = 0;
         // the output CTA expects the first message of each P stage (st.async complete_tx)
         if (rank == 1)
-            for (int i = 0; i < kPStages; ++i) mbar_arrive_expect_tx(smem_u32(&hd->p_full[i]), kMsgTx);
+            for (int i = 0; i < kPStages; ++i) mbar_arrive_expect_tx(smem_u32(&hd->p_full[i]), msg_tx<kSplit>());
         mbar_fence_init();
     }
     if (warp == kMmaWarp) {
@@ -383,6 +477,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // launched as a programmatic dependent of the prep kernel: everything above overlaps it; its
     // token records and rows are complete and visible after this wait (a no-op otherwise)
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    // the combine kernel (split KV) may be scheduled now; it waits for this grid's completion
+    if constexpr (kSplit) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const uint32_t tmem = hd->tmem_base;
     Sync sy{hd, p.status, map_to_cta(smem_u32((const void *)&hd->abort), rank ^ 1u)};
 
@@ -391,7 +487,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t *kbuf = data;
         const uint32_t kstage = (uint32_t)qch * kChunkBytes;
         if (warp >= kProdWarp0 && warp < kProdWarp0 + 4) {
-            producer(p, sy, &ori_map, &cmp_map, kbuf, hd->k_full, hd->k_empty, hd->rowbuf, kKStages, qch);
+            producer<kSplit>(p, sy, &ori_map, &cmp_map, kbuf, hd->k_full, hd->k_empty, hd->rowbuf, kKStages, qch);
         } else if (warp == kMmaWarp) {
             constexpr uint32_t idesc = idesc_f16(kBF16 ? 1u : 0u, 128, kBK, 0);
             uint32_t kc = 0, sc = 0, qc = 0;
@@ -399,12 +495,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 int t;
                 if (!tq_read(p, sy, rank, k, t)) goto done;
                 if (t < 0) break;
-                const Item it = load_item(p, t);
-                if (it.ntiles == 0) continue;
+                const Item it = load_unit<kSplit>(p, t);
+                if (it.skip || it.ntiles == 0) continue;
                 if (!wait_warp(sy, smem_u32(&hd->q_full), qc & 1)) goto done;
                 ++qc;
                 tc_fence_after();
-                for (int j = 0; j < it.ntiles; ++j, ++kc, ++sc) {
+                for (int j = it.j0; j < it.j1; ++j, ++kc, ++sc) {
                     const int ks = kc % kKStages, sb = sc & 1;
                     if (!wait_warp(sy, smem_u32(&hd->k_full[ks]), (kc / kKStages) & 1)) goto done;
                     if (!wait_warp(sy, smem_u32(&hd->s_free[sb]), ((sc >> 1) & 1) ^ 1)) goto done;
@@ -433,7 +529,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 int t;
                 if (!tq_read(p, sy, rank, k, t)) goto done;
                 if (t < 0) break;
-                const Item it = load_item(p, t);
+                const Item it = load_unit<kSplit>(p, t);
+                if (it.skip) continue;
+                t = it.t;
                 if (it.ntiles == 0) {
                     if (p.lse && h < p.N1) p.lse[(int64_t)t * p.N1 + h] = it.valid ? p.sinks[h] : 0.f;
                     continue;
@@ -461,8 +559,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 // l: sum of the unrounded P (for the LSE); lr: sum of P as rounded for the PV
                 // product, the normaliser of O (the weights of the average are then the ones used)
-                float m = sink2, l = 1.f, lr = 1.f;
-                for (int j = 0; j < it.ntiles; ++j, ++sc, ++pc) {
+                // the sink belongs to the first piece only; later pieces start empty
+                float m = it.piece == 0 ? sink2 : -INFINITY, l = it.piece == 0 ? 1.f : 0.f, lr = l;
+                for (int j = it.j0; j < it.j1; ++j, ++sc, ++pc) {
                     const int sb = sc & 1;
                     if (!wait_warp(sy, smem_u32(&hd->s_full[sb]), (sc >> 1) & 1)) goto done;
                     tc_fence_after();
@@ -495,7 +594,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
                     float alpha = 1.f;
                     bool need = false;
-                    if (j == 0) {
+                    if (j == it.j0) {  // every tile has a valid key, so mn is finite
                         const float mn = fmaxf(m, mx);
                         const float a0 = exp2f(m - mn);
                         l *= a0;
@@ -531,7 +630,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     l += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
                     lr += (sumr4[0] + sumr4[1]) + (sumr4[2] + sumr4[3]);
                     (void)need;
-                    const bool last = j == it.ntiles - 1;
+                    const bool last = j == it.j1 - 1;
                     const int ps = pc % kPStages;
                     if (!wait_warp(sy, smem_u32(&hd->p_empty[ps]), ((pc / kPStages) & 1) ^ 1, true)) goto done;
                     const uint32_t msg = msg0 + ps * kMsgBytes;
@@ -541,12 +640,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int cc = 0; cc < 8; ++cc)
                         st_async_v4(prow + ((cc ^ (h & 7)) << 4), pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2],
                                     pk[4 * cc + 3], pbar);
-                    st_async_u32(msg + kMsgAlpha + h * 4, __float_as_uint(alpha), pbar);
-                    st_async_u32(msg + kMsgL + h * 4, __float_as_uint(lr), pbar);
-                    st_async_u32(msg + kMsgM + h * 4, __float_as_uint(m), pbar);
+                    if constexpr (kSplit)
+                        st_async_v4(msg + kMsgStats + h * 16, __float_as_uint(alpha), __float_as_uint(lr),
+                                    __float_as_uint(m), __float_as_uint(l), pbar);
+                    else {
+                        st_async_u32(msg + kMsgStats + 4 * stat_index<false>(h, kMsgAlpha), __float_as_uint(alpha), pbar);
+                        st_async_u32(msg + kMsgStats + 4 * stat_index<false>(h, kMsgL), __float_as_uint(lr), pbar);
+                        st_async_u32(msg + kMsgStats + 4 * stat_index<false>(h, kMsgM), __float_as_uint(m), pbar);
+                    }
                     (void)last;
                 }
-                if (p.lse && h < p.N1) p.lse[(int64_t)t * p.N1 + h] = (m + log2f(l)) * 0.6931471805599453f;
+                if (it.np == 1 && p.lse && h < p.N1)
+                    p.lse[(int64_t)t * p.N1 + h] = (m + log2f(l)) * 0.6931471805599453f;
             }
             // every P stage must be handed back before this CTA may exit
             for (int s2 = 0; s2 < kPStages; ++s2) {
@@ -562,7 +667,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t *msgs = data + kVStages * vch * kChunkBytes;
         const uint32_t vstage = (uint32_t)vch * kChunkBytes;
         if (warp >= kProdWarp0 && warp < kProdWarp0 + 4) {
-            producer(p, sy, &ori_map, &cmp_map, vbuf, hd->v_full, hd->v_empty, hd->rowbuf, kVStages, vch);
+            producer<kSplit>(p, sy, &ori_map, &cmp_map, vbuf, hd->v_full, hd->v_empty, hd->rowbuf, kVStages, vch);
         } else if (warp == kMmaWarp) {
             const uint32_t nhalf = (uint32_t)p.Dv / 2;
             const uint32_t idesc = idesc_f16(kBF16 ? 1u : 0u, 128, nhalf, 1);
@@ -571,20 +676,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                 int t;
                 if (!tq_read(p, sy, rank, k, t)) goto done;
                 if (t < 0) break;
-                const Item it = load_item(p, t);
-                if (it.ntiles == 0) continue;
+                const Item it = load_unit<kSplit>(p, t);
+                if (it.skip || it.ntiles == 0) continue;
                 if (!wait_warp(sy, smem_u32(&hd->o_empty), (oc & 1) ^ 1)) goto done;
                 ++oc;
-                for (int j = 0; j < it.ntiles; ++j, ++vc, ++pc) {
+                for (int j = it.j0; j < it.j1; ++j, ++vc, ++pc) {
                     const int ps = pc % kPStages, vs = vc % kVStages;
                     if (!wait_warp(sy, smem_u32(&hd->p_full[ps]), (pc / kPStages) & 1, true)) goto done;
-                    if (lane == 0) mbar_arrive_expect_tx(smem_u32(&hd->p_full[ps]), kMsgTx);  // next message
+                    if (lane == 0) mbar_arrive_expect_tx(smem_u32(&hd->p_full[ps]), msg_tx<kSplit>());  // next message
                     if (!wait_warp(sy, smem_u32(&hd->v_full[vs]), (vc / kVStages) & 1)) goto done;
                     uint8_t *msg = msgs + ps * kMsgBytes;
                     bool need = false;
                     for (int i = lane; i < 128; i += 32)
-                        need |= reinterpret_cast<const float *>(msg + kMsgAlpha)[i] != 1.f;
-                    if (__any_sync(0xffffffffu, need) && j > 0) {
+                        need |= reinterpret_cast<const float *>(msg + kMsgStats)[stat_index<kSplit>(i, kMsgAlpha)] != 1.f;
+                    if (__any_sync(0xffffffffu, need) && j > it.j0) {
                         // rescale O: wait for every PV product so far, then let warps 4-7 scale the rows
                         if (lane == 0) tc_commit(smem_u32(&hd->pv_done));
                         __syncwarp();
@@ -598,11 +703,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (!wait_warp(sy, smem_u32(&hd->rs_done), rsc & 1)) goto done;
                         ++rsc;
                     }
-                    const bool last = j == it.ntiles - 1;
+                    const bool last = j == it.j1 - 1;
                     if (last) {
                         for (int i = lane; i < 128; i += 32) {
-                            hd->fin_l[i] = reinterpret_cast<const float *>(msg + kMsgL)[i];
-                            hd->fin_m[i] = reinterpret_cast<const float *>(msg + kMsgM)[i];
+                            const float *st = reinterpret_cast<const float *>(msg + kMsgStats);
+                            hd->fin_l[i] = st[stat_index<kSplit>(i, kMsgL)];
+                            if constexpr (kSplit) {
+                                hd->fin_m[i] = st[stat_index<kSplit>(i, kMsgM)];
+                                hd->fin_ls[i] = st[stat_index<kSplit>(i, kMsgLs)];
+                            }
                         }
                         __syncwarp();
                         if (lane == 0) {
@@ -621,7 +730,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 const uint64_t adesc = sdesc_sw128(pa + kk * 32, 16, 1024);
                                 const uint64_t bdesc =
                                     sdesc_sw128(vb + (hf * nhalf / 64) * kChunkBytes + kk * 2048, kChunkBytes, 1024);
-                                mma_ss(tmem + hf * nhalf, adesc, bdesc, idesc, (j > 0 || kk > 0) ? 1u : 0u);
+                                mma_ss(tmem + hf * nhalf, adesc, bdesc, idesc, (j > it.j0 || kk > 0) ? 1u : 0u);
                             }
                         }
                         tc_commit(smem_u32(&hd->v_empty[vs]));
@@ -640,7 +749,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 int t;
                 if (!tq_read(p, sy, rank, k, t)) goto done;
                 if (t < 0) break;
-                const Item it = load_item(p, t);
+                const Item it = load_unit<kSplit>(p, t);
+                if (it.skip) continue;
+                t = it.t;
                 OT *orow = reinterpret_cast<OT *>(p.out) + ((int64_t)t * p.N1 + (h < p.N1 ? h : 0)) * p.Dv;
                 if (it.ntiles == 0) {
                     if (h < p.N1)
@@ -653,7 +764,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (poll_warp(smem_u32(&hd->rs_req), rsc & 1)) {
                         ++rsc;
                         tc_fence_after();
-                        const float a = reinterpret_cast<const float *>(msgs + hd->rs_stage * kMsgBytes + kMsgAlpha)[h];
+                        const float a =
+                            reinterpret_cast<const float *>(msgs + hd->rs_stage * kMsgBytes + kMsgStats)[stat_index<kSplit>(h, kMsgAlpha)];
                         if (__any_sync(0xffffffffu, a != 1.f)) {
                             for (int c = 0; c < p.Dv / 32; ++c) {
                                 uint32_t r[32];
@@ -686,28 +798,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!wait_warp(sy, smem_u32(&hd->fin_ready), frc & 1)) goto done;
                 ++frc;
                 tc_fence_after();
-                const float inv = 1.f / hd->fin_l[h];
-                for (int c = 0; c < p.Dv / 32; ++c) {
-                    uint32_t r[32];
-                    tmem_ld32(tmem + lane_base + c * 32, r);
-                    tc_wait_ld();
-                    if (h < p.N1) {
-                        uint32_t w[16];
+                if (it.np == 1) {
+                    const float inv = 1.f / hd->fin_l[h];
+                    for (int c = 0; c < p.Dv / 32; ++c) {
+                        uint32_t r[32];
+                        tmem_ld32(tmem + lane_base + c * 32, r);
+                        tc_wait_ld();
+                        if (h < p.N1) {
+                            float x[32];
 #pragma unroll
-                        for (int k = 0; k < 16; ++k) {
-                            const float x0 = __uint_as_float(r[2 * k]) * inv, x1 = __uint_as_float(r[2 * k + 1]) * inv;
-                            if constexpr (kBF16) {
-                                __nv_bfloat162 v = __floats2bfloat162_rn(x0, x1);
-                                w[k] = *reinterpret_cast<uint32_t *>(&v);
-                            } else {
-                                __half2 v = __floats2half2_rn(x0, x1);
-                                w[k] = *reinterpret_cast<uint32_t *>(&v);
-                            }
+                            for (int k = 0; k < 32; ++k) x[k] = __uint_as_float(r[k]) * inv;
+                            store_row32<kBF16>(orow + c * 32, x);
                         }
-                        uint4 *dst = reinterpret_cast<uint4 *>(orow + c * 32);
-#pragma unroll
-                        for (int v = 0; v < 4; ++v) dst[v] = make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
                     }
+                } else if constexpr (kSplit) {
+                    write_partial(p, hd, it, tmem + lane_base);
                 }
                 tc_fence_before();
                 __syncwarp();
@@ -728,6 +833,64 @@ done:
     cluster_sync();
     tc_fence_after();
     if (warp == kMmaWarp) tmem_dealloc(tmem, kTmemCols);
+}
+
+// Merge of the pieces of split tokens (flash-decoding's LSE combine).  Block (t, h), thread =
+// 8 consecutive output columns.  With Mx = max m_i and w_i = lr_i 2^(m_i - Mx) over the token's
+// pieces in piece order: out = sum_i w_i o_i / sum_i w_i, lse = ln 2 (Mx + log2 sum_i l_i 2^(m_i - Mx)).
+// Tokens with one piece were written by the attention kernel.  Launched as a programmatic
+// dependent of it: the wait below returns once its grid has completed and its writes are visible.
+template <bool kBF16>
+__global__ void __launch_bounds__(kMaxDv / 8) combine_kernel(const TcArgs p) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int t = blockIdx.x, h = blockIdx.y;
+    const Item it = load_item(p, t);
+    const int np = it.ntiles > p.M ? min((it.ntiles + p.M - 1) / p.M, p.P) : 1;
+    if (np == 1) return;
+    const int64_t s0 = (int64_t)t * p.P;
+    const float *ps = p.part_s + (s0 * p.N1 + h) * 4;
+    const int64_t pstride = (int64_t)p.N1 * 4;
+    float mx = -INFINITY;
+    for (int i = 0; i < np; ++i) mx = fmaxf(mx, __ldcg(ps + i * pstride));
+    float wsum = 0.f, lsum = 0.f;
+    for (int i = 0; i < np; ++i) {
+        const float e = exp2f(__ldcg(ps + i * pstride) - mx);
+        wsum = __fmaf_rn(__ldcg(ps + i * pstride + 2), e, wsum);
+        lsum = __fmaf_rn(__ldcg(ps + i * pstride + 1), e, lsum);
+    }
+    const float winv = 1.f / wsum;
+    const int d0 = threadIdx.x * 8;
+    if (d0 < p.Dv) {
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        const uint16_t *po = p.part_o + (s0 * p.N1 + h) * p.Dv + d0;
+        const int64_t ostride = (int64_t)p.N1 * p.Dv;
+#pragma unroll 4
+        for (int i = 0; i < np; ++i) {
+            const float w = __ldcg(ps + i * pstride + 2) * exp2f(__ldcg(ps + i * pstride) - mx) * winv;
+            const uint4 q = __ldcg(reinterpret_cast<const uint4 *>(po + i * ostride));
+            const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int e2 = 0; e2 < 4; ++e2) {
+                const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&qw[e2]));
+                acc[2 * e2] = __fmaf_rn(f.x, w, acc[2 * e2]);
+                acc[2 * e2 + 1] = __fmaf_rn(f.y, w, acc[2 * e2 + 1]);
+            }
+        }
+        uint32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            if constexpr (kBF16) {
+                __nv_bfloat162 v = __floats2bfloat162_rn(acc[2 * k], acc[2 * k + 1]);
+                o[k] = *reinterpret_cast<uint32_t *>(&v);
+            } else {
+                __half2 v = __floats2half2_rn(acc[2 * k], acc[2 * k + 1]);
+                o[k] = *reinterpret_cast<uint32_t *>(&v);
+            }
+        }
+        uint16_t *out = reinterpret_cast<uint16_t *>(p.out) + ((int64_t)t * p.N1 + h) * p.Dv + d0;
+        *reinterpret_cast<uint4 *>(out) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    if (threadIdx.x == 0 && p.lse) p.lse[(int64_t)t * p.N1 + h] = (mx + log2f(lsum)) * 0.6931471805599453f;
 }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -773,7 +936,47 @@ bool tc_supported(const SasFwdArgs &a) {
            a.v_head_dim == 512;
 }
 
-size_t tc_workspace(const SasFwdArgs &) { return 0; }
+// Split KV for batches with at most half as many tokens as the launch has clusters: the tiles of
+// every token are cut into P pieces of M tiles, P as large as one wave of kSplitClusters clusters
+// allows with pieces of about kMinPieceTiles tiles or more, and the pieces are merged by LSE.  The
+// plan depends on the arguments alone, so the workspace size and the launch agree.  SCFA only: its
+// tile count per token is bounded by the window and top-k sizes.
+constexpr int kSplitClusters = 74;  // 148 SMs / 2
+constexpr int kMinPieceTiles = 4;
+
+struct SplitPlan {
+    int P, M;
+};
+
+SplitPlan split_plan(const SasFwdArgs &a) {
+    SplitPlan sp{1, 0};
+    // a piece costs a Q load, a pipeline fill and a partial write: split only when at least two
+    // clusters per token would otherwise idle
+    if (a.scenario != 3 || a.num_tokens <= 0 || 2 * a.num_tokens > kSplitClusters || a.kernel == SAS_KERNEL_SIMT)
+        return sp;
+    const int64_t nw = std::max<int64_t>((int64_t)a.ori_win_left + a.ori_win_right + 1, 0);
+    const int64_t est = (nw + kBK - 1) / kBK + ((int64_t)a.topk + kBK - 1) / kBK;  // >= tiles of any token
+    // as many pieces as one wave of clusters holds, of about kMinPieceTiles tiles or more
+    int64_t P = std::min<int64_t>(kSplitClusters / a.num_tokens, (est + kMinPieceTiles - 1) / kMinPieceTiles);
+    P = std::min<int64_t>(P, kMaxPieces);
+    if (P <= 1) return sp;
+    const int64_t M = (est + P - 1) / P;
+    sp.P = (int)((est + M - 1) / M);
+    sp.M = (int)M;
+    return sp.P > 1 ? sp : SplitPlan{1, 0};
+}
+
+size_t part_o_bytes(const SasFwdArgs &a, const SplitPlan &sp) {
+    return (size_t)a.num_tokens * sp.P * a.num_heads * a.v_head_dim * 2;
+}
+
+int tc_kernel_count(const SasFwdArgs &a) { return split_plan(a).P > 1 ? 2 : 1; }
+
+size_t tc_workspace(const SasFwdArgs &a) {
+    const SplitPlan sp = split_plan(a);
+    if (sp.P <= 1) return 0;
+    return part_o_bytes(a, sp) + (size_t)a.num_tokens * sp.P * a.num_heads * 4 * sizeof(float);
+}
 
 int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const void *q, const void *ori_kv,
                   const int32_t *ori_bt, const void *cmp_kv, const float *sinks, void *out, float *lse,
@@ -804,19 +1007,26 @@ int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const 
     p.scale_log2 = a.softmax_scale * 1.4426950408889634f;
     p.test_stall = (a.flags & SAS_FWD_FLAG_TEST_STALL) ? 1 : 0;
     p.counter = reinterpret_cast<int *>(ws + L.status + sas::kTokenCounterOff);
+    const SplitPlan sp = split_plan(a);
+    p.P = sp.P;
+    p.M = sp.M;
+    p.U = a.num_tokens * sp.P;
+    p.part_o = sp.P > 1 ? reinterpret_cast<uint16_t *>(ws + L.tc) : nullptr;
+    p.part_s = sp.P > 1 ? reinterpret_cast<float *>(ws + L.tc + part_o_bytes(a, sp)) : nullptr;
     CUtensorMap ori_map, cmp_map;
     int rc = make_map(&ori_map, ori_kv, p.ori_rows, a.head_dim, bf16);
     if (rc) return rc;
     rc = make_map(&cmp_map, a.scenario >= 2 ? cmp_kv : ori_kv, p.cmp_rows, a.head_dim, bf16);
     if (rc) return rc;
-    static bool attr_done[2] = {false, false};
-    const int di = bf16 ? 0 : 1;
+    // four instantiations: element type x split
+    using KernelFn = void (*)(const TcArgs, const CUtensorMap, const CUtensorMap);
+    static const KernelFn kernels[4] = {fwd_tc_kernel<true, false>, fwd_tc_kernel<true, true>,
+                                        fwd_tc_kernel<false, false>, fwd_tc_kernel<false, true>};
+    static bool attr_done[4] = {false, false, false, false};
+    const int di = (bf16 ? 0 : 2) + (p.P > 1 ? 1 : 0);
     if (!attr_done[di]) {
-        cudaError_t e = bf16 ? cudaFuncSetAttribute(fwd_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                    kSmemBytes)
-                             : cudaFuncSetAttribute(fwd_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                    kSmemBytes);
-        if (check_cuda(e)) return SAS_ERR_CUDA;
+        if (check_cuda(cudaFuncSetAttribute(kernels[di], cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes)))
+            return SAS_ERR_CUDA;
         attr_done[di] = true;
     }
     static int num_sms = 0;
@@ -825,7 +1035,7 @@ int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const 
         if (check_cuda(cudaGetDevice(&dev))) return SAS_ERR_CUDA;
         if (check_cuda(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev))) return SAS_ERR_CUDA;
     }
-    const int clusters = std::max(1, std::min(a.num_tokens, num_sms / 2));
+    const int clusters = std::max(1, std::min(p.U, num_sms / 2));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * clusters, 1, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
@@ -840,9 +1050,19 @@ int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const 
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    cudaError_t e = bf16 ? cudaLaunchKernelEx(&cfg, fwd_tc_kernel<true>, p, ori_map, cmp_map)
-                         : cudaLaunchKernelEx(&cfg, fwd_tc_kernel<false>, p, ori_map, cmp_map);
-    return check_cuda(e);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernels[di], p, ori_map, cmp_map);
+    if (check_cuda(e)) return SAS_ERR_CUDA;
+    if (p.P > 1) {
+        cudaLaunchConfig_t cc = {};
+        cc.gridDim = dim3(a.num_tokens, a.num_heads, 1);
+        cc.blockDim = dim3(kMaxDv / 8, 1, 1);
+        cc.stream = s;
+        cc.attrs = &attr[1];
+        cc.numAttrs = 1;
+        e = bf16 ? cudaLaunchKernelEx(&cc, combine_kernel<true>, p) : cudaLaunchKernelEx(&cc, combine_kernel<false>, p);
+        if (check_cuda(e)) return SAS_ERR_CUDA;
+    }
+    return SAS_OK;
 }
 
 } // namespace sas_host

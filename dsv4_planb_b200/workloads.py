@@ -217,18 +217,23 @@ def make_workload(
     )
 
 
-def config_lengths(cfg: str, seed: int = 42):
-    """``(q_lens, kv_lens, num_heads, topk)`` of a BASELINE configuration."""
+def config_lengths(cfg: str, seed: int = 42, batch=None):
+    """``(q_lens, kv_lens, num_heads, topk)`` of a BASELINE configuration.
+
+    ``batch`` overrides the request count of the decode configs c2 and c3 (same length
+    distribution), for small-batch measurements."""
     rng = np.random.default_rng(seed)
     if cfg == "c1":
         kv = rng.integers(512, 2048 + 1, size=4).tolist()
         return [1] * 4, kv, 16, 256
     if cfg == "c2":
-        kv = rng.integers(8192, 32768 + 1, size=64).tolist()
-        return [1] * 64, kv, 128, 2048
+        b = batch or 64
+        kv = rng.integers(8192, 32768 + 1, size=b).tolist()
+        return [1] * b, kv, 128, 2048
     if cfg == "c3":
-        kv = rng.integers(4096, 65536 + 1, size=32).tolist()
-        return [2] * 32, kv, 128, 2048
+        b = batch or 32
+        kv = rng.integers(4096, 65536 + 1, size=b).tolist()
+        return [2] * b, kv, 128, 2048
     if cfg == "c4":
         ctx = rng.integers(0, 16384 + 1, size=4).tolist()
         return [8192] * 4, [c + 8192 for c in ctx], 128, 2048
@@ -247,8 +252,8 @@ CONFIG_DESCRIPTIONS = {
 }
 
 
-def config_workload(cfg: str, *, seed: int = 42, device="cpu", dtype=torch.bfloat16, **kw) -> Workload:
-    q_lens, kv_lens, n1, topk = config_lengths(cfg, seed)
+def config_workload(cfg: str, *, seed: int = 42, device="cpu", dtype=torch.bfloat16, batch=None, **kw) -> Workload:
+    q_lens, kv_lens, n1, topk = config_lengths(cfg, seed, batch)
     return make_workload(
         name=cfg, q_lens=q_lens, kv_lens=kv_lens, num_heads=n1, topk=topk, seed=seed, device=device, dtype=dtype, **kw
     )

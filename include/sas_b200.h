@@ -99,6 +99,14 @@ typedef struct SasFwdArgs {
 int sas_workspace_size(const SasFwdArgs *args, size_t *bytes);
 
 /*
+ * Number of kernels one sas_forward call with `args` launches (key resolution,
+ * attention, and the split-KV combine when the tensor-core path cuts tokens
+ * into pieces), besides one workspace memset.  No counterpart in the reference
+ * API: a launch count for profilers and benchmarks.
+ */
+int sas_forward_kernel_count(const SasFwdArgs *args, int32_t *count);
+
+/*
  * The fused attention.  Replaces the JIT kernel the reference API launches
  * (api.py:372-384; inputs kernel.py:209-237): the same eleven inputs in the
  * same order, then the two outputs, then the workspace and stream.

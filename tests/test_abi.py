@@ -126,6 +126,35 @@ def test_cu_seqlens_flag(lib):
     assert ws_size(lib, a)[0] == _lib.SAS_OK
 
 
+def kernel_count(lib, a):
+    n = ctypes.c_int32(-1)
+    rc = lib.sas_forward_kernel_count(ctypes.byref(a), ctypes.byref(n))
+    return rc, n.value
+
+
+def test_kernel_count_and_split_workspace(lib):
+    # prep + attention; small SCFA batches on the tensor-core path are cut into pieces (split KV),
+    # which adds the LSE-combine kernel and per-piece partials to the workspace
+    a = good_args()  # 2 tokens: split
+    rc, n = kernel_count(lib, a)
+    assert rc == _lib.SAS_OK and n == 3
+    split_ws = ws_size(lib, a)[1]
+    a.kernel = _lib.KERNELS["simt"]
+    assert kernel_count(lib, a) == (_lib.SAS_OK, 2)
+    assert ws_size(lib, a)[1] < split_ws
+    a.kernel = _lib.KERNELS["auto"]
+    a.batch, a.num_tokens = 64, 64  # a full decode batch: one unit per token
+    assert kernel_count(lib, a) == (_lib.SAS_OK, 2)
+    a.batch, a.num_tokens = 37, 37  # the largest batch that is still split
+    assert kernel_count(lib, a) == (_lib.SAS_OK, 3)
+    a.scenario = 1  # window only: never split
+    assert kernel_count(lib, a) == (_lib.SAS_OK, 2)
+    a.scenario, a.num_tokens = 3, 0
+    assert kernel_count(lib, a) == (_lib.SAS_OK, 0)
+    a.num_tokens, a.num_heads = 4, 0
+    assert kernel_count(lib, a)[0] == _lib.SAS_ERR_INVALID_ARG
+
+
 def test_metadata_validation(lib):
     m = _lib.SasMetaArgs()
     m.num_heads_q, m.num_heads_kv, m.head_dim = 64, 1, 512

@@ -239,3 +239,28 @@ def test_full_size_decode_sampled(api, cuda_device, kernel):
         cmp_sparse_indices=wl_c.cmp_sparse_indices, cmp_ratio=wl_c.cmp_ratio, v_head_dim=wl_c.v_head_dim,
         tokens=sample)
     assert_close_to_golden(out[sample], lse[sample], ref_out[sample], ref_lse[sample], "c2 sampled")
+
+
+@pytest.mark.parametrize("batch", [1, 4, 16, 37])
+def test_split_kv_small_batches(api, cuda_device, batch):
+    """Decode batches with at most half as many tokens as the tensor-core launch has clusters
+    are cut into pieces (split KV) and merged by LSE in a second kernel.  The merged output
+    must meet the golden bars, and repeated calls must give identical bits (the merge runs
+    in piece order, whatever piece finished last)."""
+    if not tc_available():
+        pytest.skip("tensor-core path not built")
+    from dsv4_planb_b200 import workloads as W
+
+    wl = W.config_workload("c2", device=cuda_device, batch=batch)
+    out, lse = run(api, wl, "tc", cuda_device)
+    out2, lse2 = run(api, wl, "tc", cuda_device)
+    assert np.array_equal(out, out2) and np.array_equal(lse, lse2)
+    sample = sorted({0, batch // 2, batch - 1})
+    wl_c = wl.to("cpu")
+    ref_out, ref_lse, _ = O.sparse_attn_sharedkv_oracle(
+        wl_c.q, ori_kv=wl_c.ori_kv, ori_block_table=wl_c.ori_block_table, seqused_kv=wl_c.seqused_kv,
+        q_prefix=wl_c.cu_seqlens_q[:-1], act_q=wl_c.cu_seqlens_q[1:] - wl_c.cu_seqlens_q[:-1], sinks=wl_c.sinks,
+        softmax_scale=wl_c.softmax_scale, cmp_kv=wl_c.cmp_kv, cmp_block_table=wl_c.cmp_block_table,
+        cmp_sparse_indices=wl_c.cmp_sparse_indices, cmp_ratio=wl_c.cmp_ratio, v_head_dim=wl_c.v_head_dim,
+        tokens=sample)
+    assert_close_to_golden(out[sample], lse[sample], ref_out[sample], ref_lse[sample], f"split batch {batch}")
