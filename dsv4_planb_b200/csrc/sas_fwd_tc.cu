@@ -842,55 +842,66 @@ done:
 // dependent of it: the wait below returns once its grid has completed and its writes are visible.
 template <bool kBF16>
 __global__ void __launch_bounds__(kMaxDv / 8) combine_kernel(const TcArgs p) {
+    __shared__ float4 stat_s[kMaxPieces];  // per piece: m, l, lr
+    __shared__ float w_s[kMaxPieces];      // per piece: its weight in the output
+    __shared__ float lsum_s;
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const int t = blockIdx.x, h = blockIdx.y;
     const Item it = load_item(p, t);
     const int np = it.ntiles > p.M ? min((it.ntiles + p.M - 1) / p.M, p.P) : 1;
     if (np == 1) return;
     const int64_t s0 = (int64_t)t * p.P;
-    const float *ps = p.part_s + (s0 * p.N1 + h) * 4;
-    const int64_t pstride = (int64_t)p.N1 * 4;
-    float mx = -INFINITY;
-    for (int i = 0; i < np; ++i) mx = fmaxf(mx, __ldcg(ps + i * pstride));
-    float wsum = 0.f, lsum = 0.f;
-    for (int i = 0; i < np; ++i) {
-        const float e = exp2f(__ldcg(ps + i * pstride) - mx);
-        wsum = __fmaf_rn(__ldcg(ps + i * pstride + 2), e, wsum);
-        lsum = __fmaf_rn(__ldcg(ps + i * pstride + 1), e, lsum);
-    }
-    const float winv = 1.f / wsum;
-    const int d0 = threadIdx.x * 8;
-    if (d0 < p.Dv) {
-        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        const uint16_t *po = p.part_o + (s0 * p.N1 + h) * p.Dv + d0;
-        const int64_t ostride = (int64_t)p.N1 * p.Dv;
-#pragma unroll 4
+    // one round trip for the statistics of every piece
+    if ((int)threadIdx.x < np)
+        stat_s[threadIdx.x] = __ldcg(reinterpret_cast<const float4 *>(p.part_s + ((s0 + threadIdx.x) * p.N1 + h) * 4));
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float mx = -INFINITY;
+        for (int i = 0; i < np; ++i) mx = fmaxf(mx, stat_s[i].x);
+        float wsum = 0.f, lsum = 0.f;
         for (int i = 0; i < np; ++i) {
-            const float w = __ldcg(ps + i * pstride + 2) * exp2f(__ldcg(ps + i * pstride) - mx) * winv;
-            const uint4 q = __ldcg(reinterpret_cast<const uint4 *>(po + i * ostride));
-            const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-            for (int e2 = 0; e2 < 4; ++e2) {
-                const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&qw[e2]));
-                acc[2 * e2] = __fmaf_rn(f.x, w, acc[2 * e2]);
-                acc[2 * e2 + 1] = __fmaf_rn(f.y, w, acc[2 * e2 + 1]);
-            }
+            const float e = exp2f(stat_s[i].x - mx);
+            w_s[i] = stat_s[i].z * e;
+            wsum = __fmaf_rn(stat_s[i].z, e, wsum);
+            lsum = __fmaf_rn(stat_s[i].y, e, lsum);
         }
-        uint32_t o[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            if constexpr (kBF16) {
-                __nv_bfloat162 v = __floats2bfloat162_rn(acc[2 * k], acc[2 * k + 1]);
-                o[k] = *reinterpret_cast<uint32_t *>(&v);
-            } else {
-                __half2 v = __floats2half2_rn(acc[2 * k], acc[2 * k + 1]);
-                o[k] = *reinterpret_cast<uint32_t *>(&v);
-            }
-        }
-        uint16_t *out = reinterpret_cast<uint16_t *>(p.out) + ((int64_t)t * p.N1 + h) * p.Dv + d0;
-        *reinterpret_cast<uint4 *>(out) = make_uint4(o[0], o[1], o[2], o[3]);
+        const float winv = 1.f / wsum;
+        for (int i = 0; i < np; ++i) w_s[i] *= winv;
+        lsum_s = lsum;
+        if (p.lse) p.lse[(int64_t)t * p.N1 + h] = (mx + log2f(lsum)) * 0.6931471805599453f;
     }
-    if (threadIdx.x == 0 && p.lse) p.lse[(int64_t)t * p.N1 + h] = (mx + log2f(lsum)) * 0.6931471805599453f;
+    __syncthreads();
+    const int d0 = threadIdx.x * 8;
+    if (d0 >= p.Dv) return;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    const uint16_t *po = p.part_o + (s0 * p.N1 + h) * p.Dv + d0;
+    const int64_t ostride = (int64_t)p.N1 * p.Dv;
+    // the loads of eight pieces are independent and go out together
+#pragma unroll 8
+    for (int i = 0; i < np; ++i) {
+        const uint4 q = __ldcg(reinterpret_cast<const uint4 *>(po + i * ostride));
+        const float w = w_s[i];
+        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int e2 = 0; e2 < 4; ++e2) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&qw[e2]));
+            acc[2 * e2] = __fmaf_rn(f.x, w, acc[2 * e2]);
+            acc[2 * e2 + 1] = __fmaf_rn(f.y, w, acc[2 * e2 + 1]);
+        }
+    }
+    uint32_t o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        if constexpr (kBF16) {
+            __nv_bfloat162 v = __floats2bfloat162_rn(acc[2 * k], acc[2 * k + 1]);
+            o[k] = *reinterpret_cast<uint32_t *>(&v);
+        } else {
+            __half2 v = __floats2half2_rn(acc[2 * k], acc[2 * k + 1]);
+            o[k] = *reinterpret_cast<uint32_t *>(&v);
+        }
+    }
+    uint16_t *out = reinterpret_cast<uint16_t *>(p.out) + ((int64_t)t * p.N1 + h) * p.Dv + d0;
+    *reinterpret_cast<uint4 *>(out) = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
