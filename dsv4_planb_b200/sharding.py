@@ -38,7 +38,11 @@ def request_costs(q_lens: Sequence[int], kv_lens: Sequence[int], topk: int, cmp_
 
 
 def partition_requests(costs: Sequence[int], world: int) -> List[List[int]]:
-    """Longest-processing-time assignment of requests to ``world`` ranks (each list sorted)."""
+    """Longest-processing-time assignment of requests to ``world`` ranks.
+
+    Each rank's list comes in descending cost, the order in which the rank should submit its
+    requests: the attention kernel hands tokens to its clusters in index order from a dynamic
+    queue, so the long requests start first and the short ones fill the tail."""
     heap = [(0, r) for r in range(world)]
     heapq.heapify(heap)
     parts: List[List[int]] = [[] for _ in range(world)]
@@ -46,7 +50,7 @@ def partition_requests(costs: Sequence[int], world: int) -> List[List[int]]:
         load, r = heapq.heappop(heap)
         parts[r].append(b)
         heapq.heappush(heap, (load + costs[b], r))
-    return [sorted(p) for p in parts]
+    return parts
 
 
 def _compact_pool(pool: torch.Tensor, table: torch.Tensor):
@@ -60,7 +64,7 @@ def _compact_pool(pool: torch.Tensor, table: torch.Tensor):
 
 
 def shard_workload(wl: Workload, requests: Sequence[int]) -> Workload:
-    """The sub-workload of ``requests`` (original request ids, ascending)."""
+    """The sub-workload of ``requests`` (original request ids, in the order given)."""
     cu = wl.cu_seqlens_q.tolist()
     rows = [t for b in requests for t in range(cu[b], cu[b + 1])]
     row_idx = torch.tensor(rows, dtype=torch.long, device=wl.q.device)
