@@ -1,8 +1,10 @@
 // sm_100a tensor-core path of the fused sliding-window + compressed attention.
 //
-// One query token is processed by a cluster of two CTAs on two SMs that split
-// the work by role, because one SM's tensor memory cannot hold Q, S and O at
-// once (O alone, 128 heads x 512 fp32, is all 512 TMEM columns):
+// One unit of work (a query token, or a piece of one when small batches are
+// split; combine_kernel merges the pieces) is processed by a cluster of two
+// CTAs on two SMs that split the work by role, because one SM's tensor memory
+// cannot hold Q, S and O at once (O alone, 128 heads x 512 fp32, is all 512
+// TMEM columns):
 //
 //   CTA rank 0 ("score CTA")                 CTA rank 1 ("output CTA")
 //   TMEM: Q (A operand, D_qk/2 cols)         TMEM: O (128 x D_v fp32)
@@ -74,7 +76,7 @@ constexpr int kProdWarp0 = 4;
 constexpr int kProdThreads = 128;                    // warps 4-7
 constexpr int kMmaWarp = 8;
 
-// Token queue: the score CTA's producer warp 4 takes token ids from a global counter (the next one
+// Unit queue: the score CTA's producer warp 4 takes unit ids from a global counter (the next one
 // fetched while the current one runs) and publishes them to every role of both CTAs through a
 // kTq-entry ring; an entry is reused once all kTqReaders consumer warps have read it.
 constexpr int kTq = 8;
@@ -88,7 +90,7 @@ struct Hdr {
     uint64_t k_full[kKStages], k_empty[kKStages], s_full[2], s_free[2], q_full, p_empty[kPStages];
     uint64_t v_full[kVStages], v_empty[kVStages], p_full[kPStages], o_full, o_empty, rs_req, rs_done, pv_done,
         fin_ready;
-    uint64_t tq_full[kTq], tq_empty[kTq];  // token queue (tq_empty lives in the score CTA)
+    uint64_t tq_full[kTq], tq_empty[kTq];  // unit queue (tq_empty lives in the score CTA)
     volatile int tq[kTq];
     uint32_t tmem_base;
     volatile int abort;
@@ -218,18 +220,18 @@ __device__ __forceinline__ bool poll_warp(uint32_t bar, uint32_t parity) {
     return true;
 }
 
-// Token queue.  Cluster c's first token is c (every role takes it without the queue); later ones
+// Unit queue.  Cluster c's first unit is c (every role takes it without the queue); later ones
 // come from the counter, offset by the cluster count, and pass through the queue: entry k >= 1
 // lives in slot (k - 1) % kTq.
-__device__ __forceinline__ int first_token(const TcArgs &p) {
+__device__ __forceinline__ int first_unit(const TcArgs &p) {
     return (int)cluster_id_x() < p.U ? (int)cluster_id_x() : -1;
 }
 
-// Reader side (every warp of the cluster but the writer; warp-uniform): the k-th token id of this
-// cluster, or -1 once the counter has passed the last token.  False on abort / timeout.
+// Reader side (every warp of the cluster but the writer; warp-uniform): the k-th unit id of this
+// cluster, or -1 once the counter has passed the last unit.  False on abort / timeout.
 __device__ __forceinline__ bool tq_read(const TcArgs &p, const Sync &sy, uint32_t rank, uint32_t k, int &t) {
     if (k == 0) {
-        t = first_token(p);
+        t = first_unit(p);
         return true;
     }
     const int s = (k - 1) % kTq;
@@ -247,11 +249,11 @@ __device__ __forceinline__ bool tq_read(const TcArgs &p, const Sync &sy, uint32_
 }
 
 // Writer side (score CTA, warp 4; warp-uniform).  `pend` (lane 0) holds the id taken while the
-// previous token's last tiles were being gathered (-1: none yet, take one now); taking it only
-// then keeps a cluster from holding a token it cannot start soon.
+// previous unit's last tiles were being gathered (-1: none yet, take one now); taking it only
+// then keeps a cluster from holding a unit it cannot start soon.
 __device__ __forceinline__ bool tq_publish(const TcArgs &p, const Sync &sy, uint32_t k, int &pend, int &t) {
     if (k == 0) {
-        t = first_token(p);
+        t = first_unit(p);
         return true;
     }
     const int s = (k - 1) % kTq;
