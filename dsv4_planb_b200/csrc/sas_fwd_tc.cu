@@ -563,6 +563,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // product, the normaliser of O (the weights of the average are then the ones used)
                 // the sink belongs to the first piece only; later pieces start empty
                 float m = it.piece == 0 ? sink2 : -INFINITY, l = it.piece == 0 ? 1.f : 0.f, lr = l;
+                bool next_q = false;  // the next unit's Q row (and record) prefetched into L2
                 for (int j = it.j0; j < it.j1; ++j, ++sc, ++pc) {
                     const int sb = sc & 1;
                     if (!wait_warp(sy, smem_u32(&hd->s_full[sb]), (sc >> 1) & 1)) goto done;
@@ -570,6 +571,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint32_t sr[64];
                     tmem_ld32(tmem + lane_base + kTmemS + sb * kBK, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
                     tmem_ld32(tmem + lane_base + kTmemS + sb * kBK + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+                    if (!next_q) {
+                        // peek (without consuming) queue entry k + 1, published once the producer
+                        // starts that unit, a few tiles before this one ends; its Q row then comes
+                        // from L2 at the switch instead of in nine round trips to DRAM
+                        const uint32_t kn = k + 1, qs = (kn - 1) % kTq;
+                        if (mbar_test_cluster(smem_u32(&hd->tq_full[qs]), ((kn - 1) / kTq) & 1)) {
+                            const int un = hd->tq[qs];
+                            if (un >= 0) {
+                                const int tn = kSplit ? un % p.T : un;
+                                const char *qn = reinterpret_cast<const char *>(p.q) +
+                                                 ((int64_t)tn * p.N1 + (h < p.N1 ? h : 0)) * p.Dq * 2;
+                                for (int c = 0; c < p.Dq * 2; c += 128) prefetch_l2(qn + c);
+                                if (h == 0) prefetch_l2(p.tinfo + (int64_t)tn * sas::TI_INTS);
+                            }
+                            next_q = true;
+                        }
+                    }
                     tc_wait_ld();
                     tc_fence_before();
                     __syncwarp();

@@ -45,6 +45,18 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// Non-blocking test of a phase (try_wait may suspend the thread for a while; this never does).
+__device__ __forceinline__ bool mbar_test_cluster(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
 __device__ __forceinline__ bool mbar_try_cluster(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -55,6 +67,11 @@ __device__ __forceinline__ bool mbar_try_cluster(uint32_t bar, uint32_t parity) 
         : "r"(bar), "r"(parity)
         : "memory");
     return ok != 0;
+}
+
+// Fetch the 128-byte line holding `ptr` into L2 (no data returned to the SM).
+__device__ __forceinline__ void prefetch_l2(const void *ptr) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
 }
 
 // 2^x with the MUFU approximation (PTX ex2.approx.ftz.f32: ~2 ulp, subnormal results flushed
