@@ -212,7 +212,8 @@ __device__ __forceinline__ bool wait_warp(const Sync &s, uint32_t bar, uint32_t 
 // any lane sees the phase complete.  A completed phase stays complete until
 // this warp arrives elsewhere, so the lanes that lagged succeed at once.
 __device__ __forceinline__ bool poll_warp(uint32_t bar, uint32_t parity) {
-    const bool mine = mbar_try(bar, parity);
+    // test_wait never suspends: a try_wait on one barrier could sleep through the other's phase
+    const bool mine = mbar_test(bar, parity);
     if (!__any_sync(0xffffffffu, mine)) return false;
     if (!mine)
         while (!mbar_try(bar, parity)) {
