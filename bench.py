@@ -277,6 +277,12 @@ def main():
         wl = W.config_workload(args.workload, seed=42 + rank, device=dev, batch=args.batch)
     figs = algorithmic_figures(wl, dev)
     kw = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in wl.api_kwargs().items()}
+    split = 0
+    if strong:
+        # the sharding layer knows its requests' lengths: it picks the piece size that best spreads
+        # the shard's tokens over the tensor-core kernel's clusters (0: whole tokens)
+        split = S.split_hint(S.token_tiles(wl.q_lens, wl.kv_lens, wl.topk, wl.cmp_ratio))
+        kw["split_tiles"] = split
     q = wl.q
     T, N1, _ = q.shape
     Dv = wl.v_head_dim
@@ -453,12 +459,13 @@ def main():
                                + (f" (batch overridden: {args.batch} requests)" if args.batch else ""),
                    "global_batch": total_tokens if strong else T * world,
                    "per_gpu_batch": T, "seq_len": "U[8K,32K]" if args.workload == "c2" else None,
-                   "parallelism": (f"LPT request shards x{world}" if strong else f"request-sharded x{world}"), "l2": "flushed (256 MiB write) before every step",
+                   "parallelism": (f"LPT request shards x{world}" if strong else f"request-sharded x{world}"),
+                   "split_tiles": split, "l2": "flushed (256 MiB write) before every step",
                    "timing": "CUDA graph replay per step, CUDA events, max over ranks"},
         "roofline": roofline,
         "cpu_baseline": cpu,
         "e2e": e2e,
-        "gpu_launches": _kernels_per_call(wl, args.kernel) * args.steps,
+        "gpu_launches": _kernels_per_call(wl, args.kernel, split) * args.steps,
         "clocks": clocks,
         "algorithmic": {"kv_bytes": figs["kv_bytes"], "keys": figs["keys"]},
     }
@@ -480,7 +487,7 @@ def _tc_used(wl) -> bool:
     return _lib.load().sas_workspace_size(_lib.ctypes.byref(a), _lib.ctypes.byref(n)) == 0
 
 
-def _kernels_per_call(wl, kernel: str) -> int:
+def _kernels_per_call(wl, kernel: str, split_tiles: int = 0) -> int:
     """Kernels one sas_forward call on this workload launches (sas_forward_kernel_count)."""
     from dsv4_planb_b200 import _lib
 
@@ -493,6 +500,7 @@ def _kernels_per_call(wl, kernel: str) -> int:
     a.ori_win_left, a.ori_win_right, a.ori_mask_mode, a.cmp_mask_mode = 127, 0, 4, 3
     a.dtype, a.softmax_scale, a.kernel = 0, wl.softmax_scale, _lib.KERNELS[kernel]
     a.flags = _lib.SAS_FWD_FLAG_CU_SEQLENS
+    a.split_tiles = split_tiles
     n = _lib.ctypes.c_int32(0)
     _lib.check(_lib.load().sas_forward_kernel_count(_lib.ctypes.byref(a), _lib.ctypes.byref(n)), "kernel count")
     return n.value

@@ -80,7 +80,8 @@ class SasFwdArgs(ctypes.Structure):
         ("softmax_scale", ctypes.c_float),
         ("kernel", ctypes.c_int32),
         ("flags", ctypes.c_int32),
-        ("reserved", ctypes.c_int32 * 5),
+        ("split_tiles", ctypes.c_int32),
+        ("reserved", ctypes.c_int32 * 4),
     ]
 
 

@@ -83,6 +83,7 @@ def sparse_attn_sharedkv(
     out: Optional[torch.Tensor] = None,
     lse_out: Optional[torch.Tensor] = None,
     check_status: bool = False,
+    split_tiles: int = 0,
 ) -> Union[torch.Tensor, Tuple[torch.Tensor, torch.Tensor]]:
     """Sink-seeded sliding-window + compressed attention over a shared K = V cache.
 
@@ -91,6 +92,12 @@ def sparse_attn_sharedkv(
     the layout of ``q`` (last dim ``v_head_dim``), and with
     ``return_softmax_lse`` also the fp32 natural-log LSE ``[T, N1]`` (TND) or
     ``[B, S, N1]`` (BSND) with the sink folded in.
+
+    B200 extensions of the reference signature: ``kernel`` ("auto", "tc", "simt"),
+    ``max_seqlen_q`` (no host synchronisation when given), ``out`` / ``lse_out``
+    (caller-owned outputs), ``check_status`` (raise on device-side status bits) and
+    ``split_tiles`` (piece size, in 64-key tiles, for cutting long tokens across the
+    tensor-core path's clusters; 0 lets the library decide; see ``sharding.split_hint``).
     """
     del seqused_q, core_num  # API parity (the reference kernel does not read them either)
     assert ori_mask_mode == 4, "only ori_mask_mode=4 supported"
@@ -213,6 +220,9 @@ def sparse_attn_sharedkv(
     args.softmax_scale = float(softmax_scale)
     args.kernel = _lib.KERNELS[kernel]
     args.flags = _lib.SAS_FWD_FLAG_CU_SEQLENS if layout_q == "TND" else 0
+    if split_tiles < 0:
+        raise ValueError("split_tiles must be >= 0")
+    args.split_tiles = int(split_tiles)
 
     lib = _lib.load()
     nbytes = _lib.ctypes.c_size_t(0)

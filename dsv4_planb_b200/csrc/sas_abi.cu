@@ -54,7 +54,8 @@ int validate_fwd(const SasFwdArgs &a) {
     if (a.scenario == 2 && a.max_cmp_len < 0) return SAS_ERR_INVALID_ARG;
     if (a.kernel < SAS_KERNEL_AUTO || a.kernel > SAS_KERNEL_TC) return SAS_ERR_INVALID_ARG;
     if ((a.flags & ~(SAS_FWD_FLAG_CU_SEQLENS | SAS_FWD_FLAG_TEST_STALL)) != 0) return SAS_ERR_INVALID_ARG;
-    for (int i = 0; i < 5; ++i)
+    if (a.split_tiles < 0) return SAS_ERR_INVALID_ARG;
+    for (int i = 0; i < 4; ++i)
         if (a.reserved[i] != 0) return SAS_ERR_INVALID_ARG;
     if (a.kernel == SAS_KERNEL_TC && !tc_supported(a)) return SAS_ERR_UNSUPPORTED;
     return SAS_OK;

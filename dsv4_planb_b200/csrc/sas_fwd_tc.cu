@@ -982,6 +982,16 @@ struct SplitPlan {
 
 SplitPlan split_plan(const SasFwdArgs &a) {
     SplitPlan sp{1, 0};
+    if (a.split_tiles > 0 && a.scenario == 3 && a.num_tokens > 0 && a.kernel != SAS_KERNEL_SIMT) {
+        // the caller's piece size (it knows the request lengths)
+        const int64_t nw = std::max<int64_t>((int64_t)a.ori_win_left + a.ori_win_right + 1, 0);
+        const int64_t est = (nw + kBK - 1) / kBK + ((int64_t)a.topk + kBK - 1) / kBK;
+        const int64_t M = std::max<int64_t>(a.split_tiles, (est + kMaxPieces - 1) / kMaxPieces);
+        if (M >= est) return sp;
+        sp.P = (int)((est + M - 1) / M);
+        sp.M = (int)M;
+        return sp;
+    }
     // a piece costs a Q load, a pipeline fill and a partial write: split only when at least two
     // clusters per token would otherwise idle
     if (a.scenario != 3 || a.num_tokens <= 0 || 2 * a.num_tokens > kSplitClusters || a.kernel == SAS_KERNEL_SIMT)

@@ -12,7 +12,9 @@ only to bring outputs back together for verification.
   indices, lengths, and the physical blocks its block tables reference,
   compacted into a local pool with remapped tables;
 * ``gather_outputs``      ``all_gather`` of every rank's (out, lse, request ids)
-  padded to a common size, reassembled in the original token order.
+  padded to a common size, reassembled in the original token order;
+* ``split_hint``          the piece size (``split_tiles``) that best balances a
+  rank's tokens over the tensor-core kernel's clusters, by simulating its queue.
 """
 
 from __future__ import annotations
@@ -35,6 +37,60 @@ def request_costs(q_lens: Sequence[int], kv_lens: Sequence[int], topk: int, cmp_
             c += min(win, max(sg + 1, 0)) + min(topk, max((sg + 1) // cmp_ratio, 0))
         costs.append(c)
     return costs
+
+
+def token_tiles(q_lens: Sequence[int], kv_lens: Sequence[int], topk: int, cmp_ratio: int = 4,
+                win: int = 128, tile: int = 64) -> List[int]:
+    """Tiles of ``tile`` keys of every query token, in flat token order (SCFA, as the kernel counts
+    them: window tiles plus compressed tiles, assuming every top-k slot below the causal limit is
+    a valid index)."""
+    tiles = []
+    for ql, kv in zip(q_lens, kv_lens):
+        for s in range(ql):
+            sg = kv - ql + s
+            n_win = min(win, max(sg + 1, 0))
+            n_cmp = min(topk, max((sg + 1) // cmp_ratio, 0))
+            tiles.append(-(-n_win // tile) + -(-n_cmp // tile))
+    return tiles
+
+
+def queue_makespan(tiles: Sequence[int], split_tiles: int, clusters: int = 74, unit_cost: float = 2.25,
+                   piece_cost: float = 4.0) -> float:
+    """Simulated duration, in tile periods, of the tensor-core kernel's dynamic queue over
+    ``tiles``: units in the kernel's order (piece-major: the first piece of every token, then the
+    second pieces, ...), each taken by the cluster that frees first.  A unit costs its tiles plus
+    ``unit_cost`` (Q load and pipeline turn-over); a piece of a split token ``piece_cost`` more
+    (its partial output and share of the merge).  The default costs are fitted to B200 timings
+    of c5 request shards split at 12-28 tiles."""
+    pieces = []
+    for n in tiles:
+        if split_tiles and n > split_tiles:
+            k = -(-n // split_tiles)
+            pieces.append([split_tiles] * (k - 1) + [n - split_tiles * (k - 1)])
+        else:
+            pieces.append([n])
+    heap = [0.0] * clusters
+    depth = max((len(p) for p in pieces), default=0)
+    for k in range(depth):
+        for p in pieces:
+            if k < len(p):
+                cost = p[k] + unit_cost + (piece_cost if len(p) > 1 else 0.0)
+                heapq.heapreplace(heap, heap[0] + cost)
+    return max(heap) if heap else 0.0
+
+
+def split_hint(tiles: Sequence[int], clusters: int = 74, min_gain: float = 0.08) -> int:
+    """``split_tiles`` for a batch whose tokens have ``tiles`` tiles each: the piece size with the
+    shortest simulated queue, or 0 (no split) unless that beats no split by ``min_gain``."""
+    if not tiles:
+        return 0
+    base = queue_makespan(tiles, 0, clusters)
+    best, best_m = base, 0
+    for m in range(4, max(tiles)):
+        t = queue_makespan(tiles, m, clusters)
+        if t < best:
+            best, best_m = t, m
+    return best_m if best < (1.0 - min_gain) * base else 0
 
 
 def partition_requests(costs: Sequence[int], world: int) -> List[List[int]]:

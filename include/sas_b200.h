@@ -73,8 +73,23 @@ typedef struct SasFwdArgs {
     float softmax_scale;
     int32_t kernel;         /* SasKernel */
     int32_t flags;          /* SAS_FWD_FLAG_* bits (0: the reference's q_prefix / act_q_len inputs) */
-    int32_t reserved[5];    /* must be 0 */
+    int32_t split_tiles;    /* 0, or a piece size in 64-key tiles: see below */
+    int32_t reserved[4];    /* must be 0 */
 } SasFwdArgs;
+
+/*
+ * SasFwdArgs.split_tiles.  The tensor-core path processes a batch as units
+ * handed to its 74 two-SM clusters by a dynamic queue.  A unit is a whole
+ * token, or, for batches of at most 37 tokens (SCFA), a piece of one: tokens
+ * are then cut into pieces that fill the clusters and an LSE-combine kernel
+ * merges them.  A host that knows its requests' lengths (the device tensors
+ * hold them, so the library does not) may set split_tiles > 0 instead: every
+ * SCFA token with more than split_tiles tiles of 64 keys is cut into pieces of
+ * split_tiles tiles, whatever the batch size.  This balances batches of a few
+ * long and many short requests, as a request shard of a multi-GPU batch is.
+ * The workspace then holds a bf16 partial output per piece.  Ignored by the
+ * CUDA-core kernel and for the SWA and CFA scenarios.
+ */
 
 /*
  * SasFwdArgs.flags.

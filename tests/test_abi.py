@@ -155,6 +155,21 @@ def test_kernel_count_and_split_workspace(lib):
     assert kernel_count(lib, a)[0] == _lib.SAS_ERR_INVALID_ARG
 
 
+def test_split_tiles_hint(lib):
+    # a caller-chosen piece size cuts tokens whatever the batch size; negative sizes are rejected
+    a = good_args()
+    a.batch, a.num_tokens = 128, 128
+    plain = ws_size(lib, a)[1]
+    assert kernel_count(lib, a) == (_lib.SAS_OK, 2)
+    a.split_tiles = 16
+    assert kernel_count(lib, a) == (_lib.SAS_OK, 3)
+    assert ws_size(lib, a)[1] > plain
+    a.split_tiles = 64  # no token has more tiles than that: nothing to cut
+    assert kernel_count(lib, a) == (_lib.SAS_OK, 2)
+    a.split_tiles = -1
+    assert ws_size(lib, a)[0] == _lib.SAS_ERR_INVALID_ARG
+
+
 def test_metadata_validation(lib):
     m = _lib.SasMetaArgs()
     m.num_heads_q, m.num_heads_kv, m.head_dim = 64, 1, 512

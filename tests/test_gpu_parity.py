@@ -264,3 +264,32 @@ def test_split_kv_small_batches(api, cuda_device, batch):
         cmp_sparse_indices=wl_c.cmp_sparse_indices, cmp_ratio=wl_c.cmp_ratio, v_head_dim=wl_c.v_head_dim,
         tokens=sample)
     assert_close_to_golden(out[sample], lse[sample], ref_out[sample], ref_lse[sample], f"split batch {batch}")
+
+
+def test_split_tiles_hint_on_a_request_shard(api, cuda_device):
+    """A c5-style request shard (a few long and many short requests) with the sharding layer's
+    piece size: long tokens are cut across clusters and merged; parity on sampled tokens and
+    identical bits on a second call."""
+    if not tc_available():
+        pytest.skip("tensor-core path not built")
+    from dsv4_planb_b200 import sharding as S
+    from dsv4_planb_b200 import workloads as W
+
+    q_all, kv_all, n1, topk = W.config_lengths("c5", 42)
+    mine = S.partition_requests(S.request_costs(q_all, kv_all, topk), 4)[0][:96]
+    wl = W.make_workload(name="c5[shard]", q_lens=[q_all[i] for i in mine], kv_lens=[kv_all[i] for i in mine],
+                         num_heads=n1, topk=topk, seed=7, device=cuda_device)
+    split = S.split_hint(S.token_tiles(wl.q_lens, wl.kv_lens, topk))
+    assert split > 0
+    out, lse = run(api, wl, "tc", cuda_device, split_tiles=split)
+    out2, lse2 = run(api, wl, "tc", cuda_device, split_tiles=split)
+    assert np.array_equal(out, out2) and np.array_equal(lse, lse2)
+    sample = [0, 1, 40, 95]
+    wl_c = wl.to("cpu")
+    ref_out, ref_lse, _ = O.sparse_attn_sharedkv_oracle(
+        wl_c.q, ori_kv=wl_c.ori_kv, ori_block_table=wl_c.ori_block_table, seqused_kv=wl_c.seqused_kv,
+        q_prefix=wl_c.cu_seqlens_q[:-1], act_q=wl_c.cu_seqlens_q[1:] - wl_c.cu_seqlens_q[:-1], sinks=wl_c.sinks,
+        softmax_scale=wl_c.softmax_scale, cmp_kv=wl_c.cmp_kv, cmp_block_table=wl_c.cmp_block_table,
+        cmp_sparse_indices=wl_c.cmp_sparse_indices, cmp_ratio=wl_c.cmp_ratio, v_head_dim=wl_c.v_head_dim,
+        tokens=sample)
+    assert_close_to_golden(out[sample], lse[sample], ref_out[sample], ref_lse[sample], f"shard split {split}")

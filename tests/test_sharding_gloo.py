@@ -78,6 +78,25 @@ def test_partition_balances_cost():
     assert max(loads) - min(loads) <= max(costs)
 
 
+def test_rank_lists_run_largest_first():
+    costs = [5, 100, 10, 90, 80, 70, 10]
+    for p in S.partition_requests(costs, 2):
+        assert [costs[i] for i in p] == sorted((costs[i] for i in p), reverse=True)
+
+
+def test_token_tiles_and_split_hint():
+    # window tiles + compressed tiles per token, as the kernel counts them
+    assert S.token_tiles([1, 1, 2], [20000, 300, 129], 2048) == [2 + 32, 2 + 2, 2 + 1, 2 + 1]
+    # a uniform decode batch of fewer tokens than clusters gains nothing from cutting tokens
+    assert S.split_hint([34] * 64) == 0
+    # a few more long tokens than clusters: a second wave of whole long tokens; cutting them balances
+    tiles = [34] * 80 + [6] * 20
+    m = S.split_hint(tiles)
+    assert 4 <= m < 34
+    assert S.queue_makespan(tiles, m) < 0.95 * S.queue_makespan(tiles, 0)
+    assert S.queue_makespan([], 0) == 0.0 and S.split_hint([]) == 0
+
+
 def test_shard_remaps_blocks_and_keeps_rows():
     wl = _wl()
     sh = S.shard_workload(wl, [1, 3])
