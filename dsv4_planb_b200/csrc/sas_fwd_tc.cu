@@ -973,12 +973,20 @@ bool tc_supported(const SasFwdArgs &a) {
 // allows with pieces of about kMinPieceTiles tiles or more, and the pieces are merged by LSE.  The
 // plan depends on the arguments alone, so the workspace size and the launch agree.  SCFA only: its
 // tile count per token is bounded by the window and top-k sizes.
-constexpr int kSplitClusters = 74;  // 148 SMs / 2
-constexpr int kMinPieceTiles = 4;
-
 struct SplitPlan {
     int P, M;
 };
+
+constexpr int kSplitClusters = 74;  // 148 SMs / 2
+constexpr int kMinPieceTiles = 4;
+constexpr int64_t kMaxPartialBytes = int64_t(1) << 30;  // bf16 partials of a split batch, at most
+
+// A plan whose partial outputs would not fit kMaxPartialBytes falls back to whole tokens.
+SplitPlan capped(const SasFwdArgs &a, SplitPlan sp) {
+    const int64_t bytes = (int64_t)a.num_tokens * sp.P * a.num_heads * a.v_head_dim * 2;
+    return sp.P > 1 && bytes > kMaxPartialBytes ? SplitPlan{1, 0} : sp;
+}
+
 
 SplitPlan split_plan(const SasFwdArgs &a) {
     SplitPlan sp{1, 0};
@@ -990,7 +998,7 @@ SplitPlan split_plan(const SasFwdArgs &a) {
         if (M >= est) return sp;
         sp.P = (int)((est + M - 1) / M);
         sp.M = (int)M;
-        return sp;
+        return capped(a, sp);
     }
     // a piece costs a Q load, a pipeline fill and a partial write: split only when at least two
     // clusters per token would otherwise idle
@@ -1005,7 +1013,7 @@ SplitPlan split_plan(const SasFwdArgs &a) {
     const int64_t M = (est + P - 1) / P;
     sp.P = (int)((est + M - 1) / M);
     sp.M = (int)M;
-    return sp.P > 1 ? sp : SplitPlan{1, 0};
+    return sp.P > 1 ? capped(a, sp) : SplitPlan{1, 0};
 }
 
 size_t part_o_bytes(const SasFwdArgs &a, const SplitPlan &sp) {

@@ -87,7 +87,8 @@ typedef struct SasFwdArgs {
  * SCFA token with more than split_tiles tiles of 64 keys is cut into pieces of
  * split_tiles tiles, whatever the batch size.  This balances batches of a few
  * long and many short requests, as a request shard of a multi-GPU batch is.
- * The workspace then holds a bf16 partial output per piece.  Ignored by the
+ * The workspace then holds a bf16 partial output per piece; a request whose
+ * partials would exceed 1 GiB runs on whole tokens instead.  Ignored by the
  * CUDA-core kernel and for the SWA and CFA scenarios.
  */
 

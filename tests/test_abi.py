@@ -168,6 +168,9 @@ def test_split_tiles_hint(lib):
     assert kernel_count(lib, a) == (_lib.SAS_OK, 2)
     a.split_tiles = -1
     assert ws_size(lib, a)[0] == _lib.SAS_ERR_INVALID_ARG
+    # a prefill-sized batch would need more than 1 GiB of partials: whole tokens instead
+    a.split_tiles, a.batch, a.num_tokens, a.max_q_len = 16, 4, 32768, 8192
+    assert kernel_count(lib, a) == (_lib.SAS_OK, 2)
 
 
 def test_metadata_validation(lib):
