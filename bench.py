@@ -18,7 +18,8 @@ Printed by rank 0, one JSON line:
   e2e          the same metric through the public API with host buffers: per
                step, the step's inputs copied from pinned host memory, the
                call, and out + lse copied back to pinned host memory; steps
-               rotate over E2E_STREAMS CUDA streams so copies overlap compute
+               rotate over E2E_STREAMS CUDA streams so copies overlap compute,
+               and q's upload is split over E2E_COPY_STREAMS copy streams
   roofline     HBM roofline of the attention kernel (algorithmic bytes per
                launch / its CUDA-event duration vs the measured copy peak), from
                a second capture of the step with events around that kernel
@@ -47,6 +48,7 @@ import torch  # noqa: E402
 
 L2_FLUSH_BYTES = 256 << 20
 E2E_STREAMS = 3
+E2E_COPY_STREAMS = 4
 
 
 def parse():
@@ -365,28 +367,59 @@ def main():
     e2e = None
     if not args.no_e2e:
         # Every step copies its own inputs from pinned host memory, runs the public API call and
-        # reads its out + lse back into pinned host memory.  Steps rotate over E2E_STREAMS streams,
-        # so one step's copies overlap another's compute, as a serving loop would run them.
+        # reads its out + lse back into pinned host memory.  Steps rotate over E2E_STREAMS slots
+        # (a compute stream with its own device buffers), so one step's copies overlap another's
+        # compute, as a serving loop would run them.  The q upload (9.4 MB at c2) is split over
+        # E2E_COPY_STREAMS copy streams: one host-to-device copy of that size reaches only
+        # 13-30 GB/s on these hosts, four concurrent ones 35-38 GB/s.
         pin = lambda x: x.cpu().pin_memory()  # noqa: E731
         host = {"q": pin(q)}
         for k in ("cmp_sparse_indices", "cu_seqlens_q", "seqused_kv", "ori_block_table", "cmp_block_table", "sinks"):
             host[k] = pin(kw[k])
         streams = [torch.cuda.Stream(device=dev) for _ in range(E2E_STREAMS)]
+        copy_streams = [torch.cuda.Stream(device=dev) for _ in range(E2E_COPY_STREAMS)]
+        dev_in = [{k: torch.empty_like(v, device=dev) for k, v in host.items()} for _ in streams]
+        dev_out = [(torch.empty((T, N1, Dv), dtype=q.dtype, device=dev),
+                    torch.empty((T, N1), dtype=torch.float32, device=dev)) for _ in streams]
         outs_h = [(torch.empty((T, N1, Dv), dtype=q.dtype).pin_memory(),
                    torch.empty((T, N1), dtype=torch.float32).pin_memory()) for _ in streams]
+        inputs_free = [None] * len(streams)  # event after the slot's last kernel read its inputs
         h2d = sum(v.numel() * v.element_size() for v in host.values())
         d2h = outs_h[0][0].numel() * outs_h[0][0].element_size() + outs_h[0][1].numel() * outs_h[0][1].element_size()
         base = {k: v for k, v in kw.items() if not isinstance(v, torch.Tensor) or k in ("ori_kv", "cmp_kv")}
+        q_h = host["q"].view(-1)
 
         def e2e_step(i):
-            st = streams[i % len(streams)]
-            out_h, lse_h = outs_h[i % len(streams)]
+            slot = i % len(streams)
+            st = streams[slot]
+            d = dev_in[slot]
+            q_d = d["q"].view(-1)
+            chunk = -(-q_h.numel() // len(copy_streams))
+            landed = []
+            for c, cs in enumerate(copy_streams):
+                if inputs_free[slot] is not None:
+                    cs.wait_event(inputs_free[slot])
+                with torch.cuda.stream(cs):
+                    q_d[c * chunk:(c + 1) * chunk].copy_(q_h[c * chunk:(c + 1) * chunk], non_blocking=True)
+                    if c == 0:
+                        for k, v in host.items():
+                            if k != "q":
+                                d[k].copy_(v, non_blocking=True)
+                    ev = torch.cuda.Event()
+                    ev.record(cs)
+                    landed.append(ev)
+            for ev in landed:
+                st.wait_event(ev)
+            out_d, lse_d = dev_out[slot]
+            out_h, lse_h = outs_h[slot]
             with torch.cuda.stream(st):
-                d = {k: v.to(dev, non_blocking=True) for k, v in host.items()}
-                o, l_ = sparse_attn_sharedkv(d.pop("q"), return_softmax_lse=True, kernel=args.kernel,
-                                             max_seqlen_q=max_q, **d, **base)
-                out_h.copy_(o, non_blocking=True)
-                lse_h.copy_(l_, non_blocking=True)
+                sparse_attn_sharedkv(d["q"], out=out_d, lse_out=lse_d, return_softmax_lse=True, kernel=args.kernel,
+                                     max_seqlen_q=max_q, **{k: v for k, v in d.items() if k != "q"}, **base)
+                free = torch.cuda.Event()
+                free.record(st)
+                inputs_free[slot] = free
+                out_h.copy_(out_d, non_blocking=True)
+                lse_h.copy_(lse_d, non_blocking=True)
 
         for i in range(args.warmup):
             e2e_step(i)
@@ -397,7 +430,7 @@ def main():
         e1 = torch.cuda.Event(enable_timing=True)
         cur = torch.cuda.current_stream()
         e0.record(cur)
-        for st in streams:
+        for st in streams + copy_streams:
             st.wait_event(e0)
         for i in range(args.steps):
             e2e_step(i)
@@ -409,7 +442,7 @@ def main():
         if world > 1:
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
         e2e = {"value": tokens_all / (float(te.item()) / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-               "d2h_bytes_per_step": d2h, "streams": len(streams)}
+               "d2h_bytes_per_step": d2h, "streams": len(streams), "copy_streams": len(copy_streams)}
 
     # ---- roofline of the attention kernel
     peaks = measured_peaks()
