@@ -293,3 +293,27 @@ def test_split_tiles_hint_on_a_request_shard(api, cuda_device):
         cmp_sparse_indices=wl_c.cmp_sparse_indices, cmp_ratio=wl_c.cmp_ratio, v_head_dim=wl_c.v_head_dim,
         tokens=sample)
     assert_close_to_golden(out[sample], lse[sample], ref_out[sample], ref_lse[sample], f"shard split {split}")
+
+
+@pytest.mark.parametrize("dtype,heads,split", [(torch.float16, 128, 0), (torch.bfloat16, 64, 0),
+                                               (torch.float16, 64, 6)])
+def test_split_kv_dtypes_and_heads(api, cuda_device, dtype, heads, split):
+    """The split path (pieces and the combine kernel) for fp16 inputs, for fewer than 128 heads,
+    and with a caller's piece size on a batch the library would not split by itself."""
+    if not tc_available():
+        pytest.skip("tensor-core path not built")
+    from dsv4_planb_b200 import workloads as W
+
+    n = 6 if split == 0 else 48
+    wl = W.make_workload(name="split_dt", q_lens=[1] * n, kv_lens=[3000 + 977 * i for i in range(n)], num_heads=heads,
+                         topk=1024, seed=11, dtype=dtype, device=cuda_device)
+    out, lse = run(api, wl, "tc", cuda_device, split_tiles=split)
+    sample = [0, n // 2, n - 1]
+    wl_c = wl.to("cpu")
+    ref_out, ref_lse, _ = O.sparse_attn_sharedkv_oracle(
+        wl_c.q, ori_kv=wl_c.ori_kv, ori_block_table=wl_c.ori_block_table, seqused_kv=wl_c.seqused_kv,
+        q_prefix=wl_c.cu_seqlens_q[:-1], act_q=wl_c.cu_seqlens_q[1:] - wl_c.cu_seqlens_q[:-1], sinks=wl_c.sinks,
+        softmax_scale=wl_c.softmax_scale, cmp_kv=wl_c.cmp_kv, cmp_block_table=wl_c.cmp_block_table,
+        cmp_sparse_indices=wl_c.cmp_sparse_indices, cmp_ratio=wl_c.cmp_ratio, v_head_dim=wl_c.v_head_dim,
+        tokens=sample)
+    assert_close_to_golden(out[sample], lse[sample], ref_out[sample], ref_lse[sample], f"{dtype} h{heads} s{split}")
