@@ -44,6 +44,9 @@ struct FwdLayout {
 // of wall time at B200 clocks with the nanosleep back-off) before giving up.
 constexpr uint32_t kSpinLimit = 1u << 26;
 
+// Devices a process may drive (per-device launch attribute caches).
+constexpr int kMaxDevices = 64;
+
 template <typename T> struct DT;
 template <> struct DT<__nv_bfloat16> {
     static __device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }

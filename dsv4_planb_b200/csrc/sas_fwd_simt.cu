@@ -239,18 +239,21 @@ int launch_fwd_simt(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, cons
     p.scale_log2 = a.softmax_scale * 1.4426950408889634f;
     const size_t smem = simt_smem(a.head_dim);
     dim3 grid(a.num_tokens, (a.num_heads + kHG - 1) / kHG);
-    // The opt-in shared-memory size is raised once per dtype to the largest
-    // layout (D_qk = 1024), so the call inside a stream capture is a no-op.
-    static bool attr_done[2] = {false, false};
+    // The opt-in shared-memory size is raised once per device and dtype to the
+    // largest layout (D_qk = 1024), so the call inside a stream capture is a no-op.
+    int dev = 0;
+    if (check_cuda(cudaGetDevice(&dev))) return SAS_ERR_CUDA;
+    if (dev < 0 || dev >= sas::kMaxDevices) return SAS_ERR_UNSUPPORTED;
+    static bool attr_done[sas::kMaxDevices][2] = {};
     const int di = a.dtype == SAS_DTYPE_BF16 ? 0 : 1;
-    if (!attr_done[di]) {
+    if (!attr_done[dev][di]) {
         const int max_smem = (int)simt_smem(1024);
         cudaError_t e = di == 0 ? cudaFuncSetAttribute(fwd_simt_kernel<__nv_bfloat16>,
                                                        cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem)
                                 : cudaFuncSetAttribute(fwd_simt_kernel<__half>,
                                                        cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
         if (check_cuda(e)) return SAS_ERR_CUDA;
-        attr_done[di] = true;
+        attr_done[dev][di] = true;
     }
     if (a.dtype == SAS_DTYPE_BF16) fwd_simt_kernel<__nv_bfloat16><<<grid, kThreads, smem, s>>>(p);
     else fwd_simt_kernel<__half><<<grid, kThreads, smem, s>>>(p);

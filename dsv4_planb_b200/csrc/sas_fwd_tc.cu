@@ -1072,20 +1072,23 @@ int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const 
     using KernelFn = void (*)(const TcArgs, const CUtensorMap, const CUtensorMap);
     static const KernelFn kernels[4] = {fwd_tc_kernel<true, false>, fwd_tc_kernel<true, true>,
                                         fwd_tc_kernel<false, false>, fwd_tc_kernel<false, true>};
-    static bool attr_done[4] = {false, false, false, false};
+    // function attributes belong to a device's context: raised once per device and instantiation
+    // (the first call on a device must come before any stream capture)
+    int dev = 0;
+    if (check_cuda(cudaGetDevice(&dev))) return SAS_ERR_CUDA;
+    if (dev < 0 || dev >= sas::kMaxDevices) return SAS_ERR_UNSUPPORTED;
+    static uint8_t attr_done[sas::kMaxDevices] = {};
+    static int num_sms[sas::kMaxDevices] = {};
     const int di = (bf16 ? 0 : 2) + (p.P > 1 ? 1 : 0);
-    if (!attr_done[di]) {
+    if (!(attr_done[dev] & (1u << di))) {
         if (check_cuda(cudaFuncSetAttribute(kernels[di], cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes)))
             return SAS_ERR_CUDA;
-        attr_done[di] = true;
+        attr_done[dev] |= (uint8_t)(1u << di);
     }
-    static int num_sms = 0;
-    if (!num_sms) {
-        int dev = 0;
-        if (check_cuda(cudaGetDevice(&dev))) return SAS_ERR_CUDA;
-        if (check_cuda(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev))) return SAS_ERR_CUDA;
-    }
-    const int clusters = std::max(1, std::min(p.U, num_sms / 2));
+    if (!num_sms[dev] &&
+        check_cuda(cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev)))
+        return SAS_ERR_CUDA;
+    const int clusters = std::max(1, std::min(p.U, num_sms[dev] / 2));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * clusters, 1, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
