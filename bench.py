@@ -211,15 +211,15 @@ def run_reference(args, rank, world):
     torch.set_num_threads(os.cpu_count() or 1)
     wl = W.config_workload(args.workload, device="cpu", index_method="keys", batch=args.batch)
     times = []
-    tokens = 0
     per_step_budget = 4.0
     for i in range(args.warmup + args.steps):
         r = cpu_baseline(wl, budget_s=per_step_budget)
         if i >= args.warmup:
             times.append(r)
-            tokens += 0
     vals = [r["value"] for r in times if r["value"]]
     value = statistics.median(vals) if vals else None
+    # each step is a bounded sample of the workload's tokens; a whole step at the measured rate:
+    ms_per_step = wl.num_tokens / value * 1e3 if value else None
     line = {
         "impl": "reference",
         "metric": "decode tokens/s",
@@ -228,7 +228,7 @@ def run_reference(args, rank, world):
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": None,
+        "ms_per_step": ms_per_step,
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
