@@ -87,6 +87,13 @@ __device__ __forceinline__ int block_exscan(int v, int *total, int *warp_sums) {
     return before;
 }
 
+// Zeroes the status word and the token records (n16 16-byte words), then lets the prep grid launch.
+__global__ void __launch_bounds__(kThreads) clear_kernel(uint4 *words, int64_t n16) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < n16; i += (int64_t)gridDim.x * kThreads)
+        words[i] = make_uint4(0, 0, 0, 0);
+}
+
 template <int kPer>
 __global__ void __launch_bounds__(kThreads, 1) prep_kernel(PrepArgs p) {
     __shared__ int32_t tab_s[kTableSmem];
@@ -112,6 +119,9 @@ __global__ void __launch_bounds__(kThreads, 1) prep_kernel(PrepArgs p) {
         const int i = tid + k * kThreads;
         tabv[k] = staged && i < p.cmp_table_len ? __ldg(p.cmp_bt + (int64_t)b * p.cmp_table_len + i) : 0;
     }
+    // launched as a programmatic dependent of clear_kernel: the status word and the token records
+    // are zero after this wait (the request-level loads above already overlap the clear)
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     if (s == 0 && tid == 0 && aq > p.max_q_len) sas::set_status(p.status, SAS_STATUS_BAD_TOKEN);
     if (s >= aq) return;
     const int64_t t = (int64_t)q0 + s;
@@ -205,10 +215,14 @@ namespace sas_host {
 int launch_prep(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const int32_t *cmp_bt, const int32_t *idx,
                 const int32_t *q_prefix, const int32_t *act_q, const int32_t *act_kv, cudaStream_t s) {
     const bool cu = (a.flags & SAS_FWD_FLAG_CU_SEQLENS) != 0;
-    // the status word and the token records are adjacent: one memset clears both
+    // the status word and the token records are adjacent: one kernel clears both, and prep follows
+    // it as a programmatic dependent (its launch and first loads overlap the clear)
     static_assert(sizeof(int32_t) * sas::TI_INTS % 16 == 0, "token record size");
     const size_t clear = L.token_info + sizeof(int32_t) * sas::TI_INTS * (size_t)(a.num_tokens > 0 ? a.num_tokens : 0);
-    if (check_cuda(cudaMemsetAsync(ws + L.status, 0, clear - L.status, s))) return SAS_ERR_CUDA;
+    const int64_t n16 = (int64_t)((clear - L.status) / 16);
+    const int cblocks = (int)std::min<int64_t>((n16 + kThreads - 1) / kThreads, 148);
+    clear_kernel<<<cblocks, kThreads, 0, s>>>(reinterpret_cast<uint4 *>(ws + L.status), n16);
+    if (check_cuda(cudaGetLastError())) return SAS_ERR_CUDA;
     if (a.batch == 0 || a.max_q_len == 0 || a.num_tokens == 0) return SAS_OK;
     PrepArgs p;
     p.B = a.batch;
@@ -232,10 +246,18 @@ int launch_prep(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const in
     p.tinfo = reinterpret_cast<int32_t *>(ws + L.token_info);
     p.rows = reinterpret_cast<int32_t *>(ws + L.cmp_rows);
     p.status = reinterpret_cast<uint32_t *>(ws + L.status);
-    dim3 grid(a.max_q_len, a.batch);
-    if (a.scenario == 3 && a.topk > kThreads * 4) prep_kernel<8><<<grid, kThreads, 0, s>>>(p);
-    else prep_kernel<4><<<grid, kThreads, 0, s>>>(p);
-    return check_cuda(cudaGetLastError());
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.max_q_len, a.batch, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = (a.scenario == 3 && a.topk > kThreads * 4) ? cudaLaunchKernelEx(&cfg, prep_kernel<8>, p)
+                                                                      : cudaLaunchKernelEx(&cfg, prep_kernel<4>, p);
+    return check_cuda(e);
 }
 
 } // namespace sas_host
