@@ -126,10 +126,11 @@ int sas_forward_kernel_count(const SasFwdArgs *args, int32_t *count) {
     const SasFwdArgs &a = *args;
     int rc = validate_fwd(a);
     if (rc) return rc;
+    const int clear = 1;  // the status word and token records, always
     const int prep = (a.batch == 0 || a.max_q_len == 0 || a.num_tokens == 0) ? 0 : 1;
     int attn = 0;
     if (a.num_tokens > 0) attn = use_tc(a) ? tc_kernel_count(a) : (a.num_heads > 0 ? 1 : 0);
-    *count = prep + attn;
+    *count = clear + prep + attn;
     return SAS_OK;
 }
 

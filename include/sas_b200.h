@@ -115,10 +115,11 @@ typedef struct SasFwdArgs {
 int sas_workspace_size(const SasFwdArgs *args, size_t *bytes);
 
 /*
- * Number of kernels one sas_forward call with `args` launches (key resolution,
- * attention, and the split-KV combine when the tensor-core path cuts tokens
- * into pieces), besides one workspace memset.  No counterpart in the reference
- * API: a launch count for profilers and benchmarks.
+ * Number of kernels one sas_forward call with `args` launches: the clear of the
+ * workspace's status word and token records, key resolution, attention, and
+ * the split-KV combine when the tensor-core path cuts tokens into pieces.  No
+ * counterpart in the reference API: a launch count for profilers and
+ * benchmarks.
  */
 int sas_forward_kernel_count(const SasFwdArgs *args, int32_t *count);
 

@@ -133,24 +133,24 @@ def kernel_count(lib, a):
 
 
 def test_kernel_count_and_split_workspace(lib):
-    # prep + attention; small SCFA batches on the tensor-core path are cut into pieces (split KV),
-    # which adds the LSE-combine kernel and per-piece partials to the workspace
+    # clear + prep + attention; small SCFA batches on the tensor-core path are cut into pieces
+    # (split KV), which adds the LSE-combine kernel and per-piece partials to the workspace
     a = good_args()  # 2 tokens: split
     rc, n = kernel_count(lib, a)
-    assert rc == _lib.SAS_OK and n == 3
+    assert rc == _lib.SAS_OK and n == 4
     split_ws = ws_size(lib, a)[1]
     a.kernel = _lib.KERNELS["simt"]
-    assert kernel_count(lib, a) == (_lib.SAS_OK, 2)
+    assert kernel_count(lib, a) == (_lib.SAS_OK, 3)
     assert ws_size(lib, a)[1] < split_ws
     a.kernel = _lib.KERNELS["auto"]
     a.batch, a.num_tokens = 64, 64  # a full decode batch: one unit per token
-    assert kernel_count(lib, a) == (_lib.SAS_OK, 2)
-    a.batch, a.num_tokens = 37, 37  # the largest batch that is still split
     assert kernel_count(lib, a) == (_lib.SAS_OK, 3)
+    a.batch, a.num_tokens = 37, 37  # the largest batch that is still split
+    assert kernel_count(lib, a) == (_lib.SAS_OK, 4)
     a.scenario = 1  # window only: never split
-    assert kernel_count(lib, a) == (_lib.SAS_OK, 2)
-    a.scenario, a.num_tokens = 3, 0
-    assert kernel_count(lib, a) == (_lib.SAS_OK, 0)
+    assert kernel_count(lib, a) == (_lib.SAS_OK, 3)
+    a.scenario, a.num_tokens = 3, 0  # only the status word is cleared
+    assert kernel_count(lib, a) == (_lib.SAS_OK, 1)
     a.num_tokens, a.num_heads = 4, 0
     assert kernel_count(lib, a)[0] == _lib.SAS_ERR_INVALID_ARG
 
@@ -160,17 +160,17 @@ def test_split_tiles_hint(lib):
     a = good_args()
     a.batch, a.num_tokens = 128, 128
     plain = ws_size(lib, a)[1]
-    assert kernel_count(lib, a) == (_lib.SAS_OK, 2)
-    a.split_tiles = 16
     assert kernel_count(lib, a) == (_lib.SAS_OK, 3)
+    a.split_tiles = 16
+    assert kernel_count(lib, a) == (_lib.SAS_OK, 4)
     assert ws_size(lib, a)[1] > plain
     a.split_tiles = 64  # no token has more tiles than that: nothing to cut
-    assert kernel_count(lib, a) == (_lib.SAS_OK, 2)
+    assert kernel_count(lib, a) == (_lib.SAS_OK, 3)
     a.split_tiles = -1
     assert ws_size(lib, a)[0] == _lib.SAS_ERR_INVALID_ARG
     # a prefill-sized batch would need more than 1 GiB of partials: whole tokens instead
     a.split_tiles, a.batch, a.num_tokens, a.max_q_len = 16, 4, 32768, 8192
-    assert kernel_count(lib, a) == (_lib.SAS_OK, 2)
+    assert kernel_count(lib, a) == (_lib.SAS_OK, 3)
 
 
 def test_metadata_validation(lib):
