@@ -317,3 +317,61 @@ def test_split_kv_dtypes_and_heads(api, cuda_device, dtype, heads, split):
         cmp_sparse_indices=wl_c.cmp_sparse_indices, cmp_ratio=wl_c.cmp_ratio, v_head_dim=wl_c.v_head_dim,
         tokens=sample)
     assert_close_to_golden(out[sample], lse[sample], ref_out[sample], ref_lse[sample], f"{dtype} h{heads} s{split}")
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_rows_outside_every_request_are_zero(api, cuda_device, kernel):
+    """Query rows that belong to no request (BSND padding past a request's cu_seqlens_q length,
+    TND rows past the last request) are in no unit of the tensor-core kernel's longest-first
+    order: they must still come back as zero output and zero LSE, and the covered rows must
+    equal the call without padding.  The output memory is poisoned first, so a row that no
+    kernel writes shows up."""
+    if kernel == "tc" and not tc_available():
+        pytest.skip("tensor-core path not built")
+    from dsv4_planb_b200 import workloads as W
+
+    dev = cuda_device
+    q_lens = [3, 1, 2]
+    wl = W.make_workload(name="pad", q_lens=q_lens, kv_lens=[700, 1500, 2600], num_heads=128, topk=256, seed=5)
+    ref_out, ref_lse = run(api, wl, kernel, dev)
+    kw = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in wl.api_kwargs().items()}
+    T, N1, D = wl.q.shape
+    K = wl.cmp_sparse_indices.shape[-1]
+
+    def poison():
+        junk = torch.full((4 * T * N1 * 512,), float("nan"), dtype=torch.float32, device=dev)
+        del junk
+
+    # BSND, padded to 3 rows per request; cu_seqlens_q gives the real lengths
+    S = max(q_lens)
+    q_b = torch.zeros((len(q_lens), S, N1, D), dtype=wl.q.dtype, device=dev)
+    i_b = torch.full((len(q_lens), S, 1, K), -1, dtype=torch.int32, device=dev)
+    t0 = 0
+    for b, n in enumerate(q_lens):
+        q_b[b, :n] = wl.q[t0:t0 + n].to(dev)
+        i_b[b, :n] = kw["cmp_sparse_indices"][t0:t0 + n].to(torch.int32)
+        t0 += n
+    kb = dict(kw, layout_q="BSND", cmp_sparse_indices=i_b)
+    poison()
+    out_b, lse_b = api.sparse_attn_sharedkv(q_b, return_softmax_lse=True, kernel=kernel, check_status=True, **kb)
+    torch.cuda.synchronize()
+    out_b, lse_b = out_b.float().cpu().numpy(), lse_b.cpu().numpy()
+    t0 = 0
+    for b, n in enumerate(q_lens):
+        np.testing.assert_array_equal(out_b[b, :n], ref_out[t0:t0 + n])
+        np.testing.assert_array_equal(lse_b[b, :n], ref_lse[t0:t0 + n])
+        assert not out_b[b, n:].any() and not lse_b[b, n:].any(), f"padding rows of request {b}"
+        t0 += n
+
+    # TND with two rows after the last request
+    q_t = torch.cat([wl.q.to(dev), torch.randn((2, N1, D), device=dev).to(wl.q.dtype)])
+    i_t = torch.cat([kw["cmp_sparse_indices"], torch.zeros((2,) + tuple(kw["cmp_sparse_indices"].shape[1:]),
+                                                           dtype=kw["cmp_sparse_indices"].dtype, device=dev)])
+    poison()
+    out_t, lse_t = api.sparse_attn_sharedkv(q_t, return_softmax_lse=True, kernel=kernel, check_status=True,
+                                            **dict(kw, cmp_sparse_indices=i_t))
+    torch.cuda.synchronize()
+    out_t, lse_t = out_t.float().cpu().numpy(), lse_t.cpu().numpy()
+    np.testing.assert_array_equal(out_t[:T], ref_out)
+    np.testing.assert_array_equal(lse_t[:T], ref_lse)
+    assert not out_t[T:].any() and not lse_t[T:].any()
