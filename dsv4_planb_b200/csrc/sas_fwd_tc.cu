@@ -76,6 +76,25 @@ constexpr int kProdWarp0 = 4;
 constexpr int kProdThreads = 128;                    // warps 4-7
 constexpr int kMmaWarp = 8;
 
+// Q of a unit's token enters the score CTA in two parts.  Dims [0, 512): eight 64-dim chunks of
+// all 128 head rows, loaded by TMA into two K-ring stages (four chunks a stage, each chunk as two
+// 64-row boxes in adjacent slabs, so a chunk is one 128-row SW128 K-major matrix) and copied into
+// TMEM by the MMA warp with tcgen05.cp.  Dims [512, D_qk) (the rope part of D_qk 576): loaded by
+// the softmax warps, one row per thread, and stored with tcgen05.st.
+constexpr int kQTmaChunks = 8;
+constexpr int kQStages = 2;
+constexpr int kQChunksPerStage = kQTmaChunks / kQStages;
+constexpr uint32_t kQStageBytes = 2 * kQChunksPerStage * kChunkBytes;  // 64 KiB: eight 64x64 boxes
+static_assert(kKStages > kQStages, "a K tile must fit beside the Q stages");
+// Exception: a cluster's first unit of kQRegMinTiles tiles or more loads all of Q through the
+// softmax warps' registers.  At the start the gather of K bounds such a unit, and the register
+// path (nine round trips, off the TMA unit) hides behind three stages of K, where the TMA path
+// would hold two of them.  Later units' Q by TMA overlaps the previous unit's last tiles.
+// Measured, kernel time, first unit by registers / by TMA: one 34-tile token a cluster (c2)
+// 98.8 / 101.1 us; decode pieces of 9 tiles (B=16) 49.0 / 47.2 us.  The threshold sits between.
+constexpr int kQRegMinTiles = 20;
+__device__ __forceinline__ bool q_by_tma(int tiles, bool first) { return !first || tiles < kQRegMinTiles; }
+
 // Unit queue: the score CTA's producer warp 4 takes unit ids from a global counter (the next one
 // fetched while the current one runs) and publishes them to every role of both CTAs through a
 // kTq-entry ring; an entry is reused once all kTqReaders consumer warps have read it.
@@ -328,13 +347,15 @@ __device__ __forceinline__ int32_t key_row(const TcArgs &p, const Item &it, int 
 // (~40 vs ~30 GB/s in isolation; 113 vs 121 us for the kernel).
 template <bool kSplit>
 __device__ void producer(const TcArgs &p, const Sync &sy, const CUtensorMap *ori_map, const CUtensorMap *cmp_map,
-                         uint8_t *ring, uint64_t *full, uint64_t *empty, int32_t (*rowbuf)[kBK], int stages, int nch) {
+                         const CUtensorMap *q_map, uint8_t *ring, uint64_t *full, uint64_t *empty,
+                         int32_t (*rowbuf)[kBK], int stages, int nch) {
     const int pt = threadIdx.x - kProdWarp0 * 32;
     const int slab = pt >> 4, quad = pt & 15, lane = pt & 31;
     const uint32_t stage_bytes = (uint32_t)nch * kChunkBytes;
     uint32_t cnt = 0;
     const bool writer = cluster_rank() == 0 && (pt >> 5) == 0;
     int pend = -1;
+    bool first = true;  // no unit with tiles started yet
     for (uint32_t k = 0;; ++k) {
         int t = -1;
         const bool got = writer ? tq_publish(p, sy, k, pend, t) : tq_read(p, sy, cluster_rank(), k, t);
@@ -344,6 +365,24 @@ __device__ void producer(const TcArgs &p, const Sync &sy, const CUtensorMap *ori
         if (it.skip) continue;
         const int32_t *crow = p.rows + (int64_t)it.t * p.row_cap;
         int32_t fetched = pt < kBK && it.j1 > it.j0 ? key_fetch(p, it, crow, it.j0, pt) : -1;
+        const bool q_tma = q_by_tma(it.j1 - it.j0, first);
+        if (it.j1 > it.j0) first = false;
+        if (q_map != nullptr && it.j1 > it.j0 && q_tma) {
+            // score CTA: the unit's Q, dims [0, 512), into the next two stages (slab 2i + half of
+            // a stage = chunk i of the stage, heads 64 half .. 64 half + 63; rows past the last
+            // token read zeros)
+            for (int r = 0; r < kQStages; ++r) {
+                const int st = cnt % stages;
+                const uint32_t fb = smem_u32(&full[st]);
+                const bool ok = wait_warp(sy, smem_u32(&empty[st]), ((cnt / stages) & 1) ^ 1);
+                if (ok && pt == 0) mbar_arrive_expect_tx(fb, kQStageBytes);
+                if (!bar_red_and(2, kProdThreads, ok)) return;
+                if (pt < 2 * kQChunksPerStage)
+                    tma_load_2d(smem_u32(ring + (size_t)st * stage_bytes) + pt * kChunkBytes, q_map,
+                                (kQChunksPerStage * r + (pt >> 1)) * 64, it.t * p.N1 + (pt & 1) * 64, fb);
+                ++cnt;
+            }
+        }
         for (int j = it.j0; j < it.j1; ++j) {
             const int st = cnt % stages;
             const uint32_t fb = smem_u32(&full[st]);
@@ -425,7 +464,7 @@ __device__ void write_partial(const TcArgs &p, const Hdr *hd, const Item &it, ui
 template <bool kBF16, bool kSplit>
 __global__ void __launch_bounds__(kThreads, 1)
     fwd_tc_kernel(const TcArgs p, const __grid_constant__ CUtensorMap ori_map,
-                  const __grid_constant__ CUtensorMap cmp_map) {
+                  const __grid_constant__ CUtensorMap cmp_map, const __grid_constant__ CUtensorMap q_map) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     Hdr *hd = reinterpret_cast<Hdr *>(smem);
@@ -490,16 +529,42 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t *kbuf = data;
         const uint32_t kstage = (uint32_t)qch * kChunkBytes;
         if (warp >= kProdWarp0 && warp < kProdWarp0 + 4) {
-            producer<kSplit>(p, sy, &ori_map, &cmp_map, kbuf, hd->k_full, hd->k_empty, hd->rowbuf, kKStages, qch);
+            producer<kSplit>(p, sy, &ori_map, &cmp_map, &q_map, kbuf, hd->k_full, hd->k_empty, hd->rowbuf, kKStages,
+                             qch);
         } else if (warp == kMmaWarp) {
             constexpr uint32_t idesc = idesc_f16(kBF16 ? 1u : 0u, 128, kBK, 0);
             uint32_t kc = 0, sc = 0, qc = 0;
+            bool first = true;
             for (uint32_t k = 0;; ++k) {
                 int t;
                 if (!tq_read(p, sy, rank, k, t)) goto done;
                 if (t < 0) break;
                 const Item it = load_unit<kSplit>(p, t);
                 if (it.skip || it.ntiles == 0) continue;
+                const bool q_tma = q_by_tma(it.j1 - it.j0, first);
+                first = false;
+                // Q dims [0, 512) from the two stages the producer filled -> TMEM columns [0, 256).
+                // The previous unit's QK products read those columns: the copy waits for the last
+                // of them (tcgen05.cp is ordered before later MMAs, not after earlier ones).
+                if (q_tma) {
+                    for (int r = 0; r < kQStages; ++r)
+                        if (!wait_warp(sy, smem_u32(&hd->k_full[(kc + r) % kKStages]), ((kc + r) / kKStages) & 1))
+                            goto done;
+                    if (sc > 0 && !wait_warp(sy, smem_u32(&hd->s_full[(sc - 1) & 1]), ((sc - 1) >> 1) & 1)) goto done;
+                    tc_fence_after();
+                    if (lane == 0) {
+                        for (int r = 0; r < kQStages; ++r) {
+                            const uint32_t qb = smem_u32(kbuf + (size_t)((kc + r) % kKStages) * kstage);
+                            for (int i = 0; i < kQChunksPerStage; ++i)
+                                for (int kq = 0; kq < 4; ++kq)
+                                    tmem_cp_128x256b(tmem + ((kQChunksPerStage * r + i) * 4 + kq) * 8,
+                                                     sdesc_sw128(qb + 2 * i * kChunkBytes + kq * 32, 16, 1024));
+                        }
+                        for (int r = 0; r < kQStages; ++r) tc_commit(smem_u32(&hd->k_empty[(kc + r) % kKStages]));
+                    }
+                    __syncwarp();
+                    kc += kQStages;
+                }
                 if (!wait_warp(sy, smem_u32(&hd->q_full), qc & 1)) goto done;
                 ++qc;
                 tc_fence_after();
@@ -528,6 +593,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t pfull0 = map_to_cta(smem_u32(&hd->p_full[0]), 1);  // the output CTA's barriers
             const float sink2 = h < p.N1 ? p.sinks[h] * 1.4426950408889634f : 0.f;
             uint32_t sc = 0, pc = 0;
+            bool first = true;
             for (uint32_t k = 0;; ++k) {
                 int t;
                 if (!tq_read(p, sy, rank, k, t)) goto done;
@@ -539,11 +605,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (p.lse && h < p.N1) p.lse[(int64_t)t * p.N1 + h] = it.valid ? p.sinks[h] : 0.f;
                     continue;
                 }
-                // ---- Q row h -> TMEM (A operand: 2 elements per 32-bit column)
+                // ---- Q row h -> TMEM (A operand: 2 elements per 32-bit column): dims [512, D_qk),
+                // or all of them for a long first unit; dims [0, 512) otherwise come through the K
+                // ring and tcgen05.cp
                 {
+                    const bool q_tma = q_by_tma(it.j1 - it.j0, first);
+                    first = false;
                     const uint4 *qrow = reinterpret_cast<const uint4 *>(
                         reinterpret_cast<const uint16_t *>(p.q) + ((int64_t)t * p.N1 + (h < p.N1 ? h : 0)) * p.Dq);
-                    for (int c = 0; c < qch; ++c) {
+                    for (int c = q_tma ? kQTmaChunks : 0; c < qch; ++c) {
                         uint32_t r[32];
 #pragma unroll
                         for (int v = 0; v < 8; ++v) {
@@ -688,7 +758,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t *msgs = data + kVStages * vch * kChunkBytes;
         const uint32_t vstage = (uint32_t)vch * kChunkBytes;
         if (warp >= kProdWarp0 && warp < kProdWarp0 + 4) {
-            producer<kSplit>(p, sy, &ori_map, &cmp_map, vbuf, hd->v_full, hd->v_empty, hd->rowbuf, kVStages, vch);
+            producer<kSplit>(p, sy, &ori_map, &cmp_map, nullptr, vbuf, hd->v_full, hd->v_empty, hd->rowbuf, kVStages,
+                             vch);
         } else if (warp == kMmaWarp) {
             const uint32_t nhalf = (uint32_t)p.Dv / 2;
             const uint32_t idesc = idesc_f16(kBF16 ? 1u : 0u, 128, nhalf, 1);
@@ -943,13 +1014,13 @@ EncodeTiledFn encode_fn() {
 
 // Row-gather tensor map over a paged pool viewed as [rows, D] (box: 64 columns x 1 row, 128-byte
 // swizzle).  Row `rows` (one past the end) lies outside the map and reads as zeros.
-int make_map(CUtensorMap *map, const void *base, int64_t rows, int D, bool bf16) {
+int make_map(CUtensorMap *map, const void *base, int64_t rows, int D, bool bf16, uint32_t box_rows = 1) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return SAS_ERR_CUDA;
     if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || rows >= INT32_MAX) return SAS_ERR_INVALID_ARG;
     cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)D * 2};
-    cuuint32_t box[2] = {64, 1};
+    cuuint32_t box[2] = {64, box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
                     const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -1068,8 +1139,11 @@ int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const 
     if (rc) return rc;
     rc = make_map(&cmp_map, a.scenario >= 2 ? cmp_kv : ori_kv, p.cmp_rows, a.head_dim, bf16);
     if (rc) return rc;
+    CUtensorMap q_map;  // q as [T * N1 rows][D_qk], boxes of 64 dims x 64 head rows
+    rc = make_map(&q_map, q, (int64_t)a.num_tokens * a.num_heads, a.head_dim, bf16, 64);
+    if (rc) return rc;
     // four instantiations: element type x split
-    using KernelFn = void (*)(const TcArgs, const CUtensorMap, const CUtensorMap);
+    using KernelFn = void (*)(const TcArgs, const CUtensorMap, const CUtensorMap, const CUtensorMap);
     static const KernelFn kernels[4] = {fwd_tc_kernel<true, false>, fwd_tc_kernel<true, true>,
                                         fwd_tc_kernel<false, false>, fwd_tc_kernel<false, true>};
     // function attributes belong to a device's context: raised once per device and instantiation
@@ -1103,7 +1177,7 @@ int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const 
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kernels[di], p, ori_map, cmp_map);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernels[di], p, ori_map, cmp_map, q_map);
     if (check_cuda(e)) return SAS_ERR_CUDA;
     if (p.P > 1) {
         cudaLaunchConfig_t cc = {};

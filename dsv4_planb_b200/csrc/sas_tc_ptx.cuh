@@ -161,7 +161,21 @@ __device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap *map
         : "memory");
 }
 
+// ---- TMA: one box of a 2-D tensor map into shared memory (no multicast) ---------
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int32_t x, int32_t y, uint32_t bar) {
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+                     dst),
+                 "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+                 : "memory");
+}
+
 // ---- tcgen05 -----------------------------------------------------------------
+// Copy a K-major shared-memory matrix of 128 rows x 32 bytes (smem descriptor `sdesc`, the
+// operand format of the MMA) into TMEM: row r to lane r, its 32 bytes to 8 columns from `taddr`.
+// Ordered before the tcgen05.mma ops the same thread issues later; not after earlier ones.
+__device__ __forceinline__ void tmem_cp_128x256b(uint32_t taddr, uint64_t sdesc) {
+    asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
                  : "memory");

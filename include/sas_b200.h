@@ -143,6 +143,9 @@ int sas_forward_kernel_count(const SasFwdArgs *args, int32_t *count);
  *                their own split over 148 SMs, so it is not read.
  *   out          [T, N1, D_v] dtype; rows of no (b, s < act_q_len[b]) are zeroed
  *   lse          [T, N1] fp32 natural-log LSE (sink folded in), or NULL
+ * All tensors are dense.  The tensor-core kernel reads q, ori_kv and cmp_kv
+ * through TMA tensor maps: their base addresses must be 16-byte aligned, else
+ * the call returns SAS_ERR_INVALID_ARG.
  */
 int sas_forward(const SasFwdArgs *args, const void *q, const void *ori_kv, const int32_t *ori_block_table,
                 const void *cmp_kv, const int32_t *cmp_block_table, const int32_t *cmp_indices,
