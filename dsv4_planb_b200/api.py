@@ -44,6 +44,14 @@ def _i32(t: torch.Tensor, device) -> torch.Tensor:
     return t.to(device=device, dtype=torch.int32).contiguous()
 
 
+def _dense16(t: torch.Tensor) -> torch.Tensor:
+    """Contiguous, with a 16-byte aligned base: the kernels move rows in 16-byte vectors and the
+    tensor-core kernel reads q and the pools through TMA tensor maps.  A view that starts inside a
+    vector (an odd element offset) is copied; the C ABI rejects such a pointer."""
+    t = t.contiguous()
+    return t if t.data_ptr() % 16 == 0 else t.clone()
+
+
 def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
     return None if t is None else t.data_ptr()
 
@@ -173,7 +181,7 @@ def sparse_attn_sharedkv(
     if ori_kv.dtype != q.dtype or (cmp_kv is not None and cmp_kv.dtype != q.dtype):
         raise ValueError("q, ori_kv and cmp_kv must share one dtype")
 
-    ori_kv_d = ori_kv.to(dev).contiguous()
+    ori_kv_d = _dense16(ori_kv.to(dev))
     ori_bt = _i32(ori_block_table, dev)
     if ori_bt.dim() != 2 or ori_bt.shape[0] < B:
         raise ValueError(f"ori_block_table must be [B>={B}, table_len] (got {tuple(ori_bt.shape)})")
@@ -182,7 +190,7 @@ def sparse_attn_sharedkv(
     if idx_flat is not None and (idx_flat.dim() != 3 or idx_flat.shape[0] != T):
         raise ValueError(f"cmp_sparse_indices must hold one row per query token (got {tuple(idx_flat.shape)})")
     if scenario >= 2:
-        cmp_kv_d = cmp_kv.to(dev).contiguous()
+        cmp_kv_d = _dense16(cmp_kv.to(dev))
         cmp_bt = _i32(cmp_block_table, dev)
         cmp_ratio_eff = int(cmp_ratio) if cmp_ratio is not None else 4
     else:
@@ -228,15 +236,18 @@ def sparse_attn_sharedkv(
     nbytes = _lib.ctypes.c_size_t(0)
     _lib.check(lib.sas_workspace_size(_lib.ctypes.byref(args), _lib.ctypes.byref(nbytes)), "sas_workspace_size")
     ws = _workspace(nbytes.value, dev)
+    out_user = None  # a caller's out that starts inside a 16-byte vector: written through a copy
     if out is None:
         out_flat = torch.empty((T, N1, Dv), dtype=q.dtype, device=dev)
     else:
         out_flat = out.view(T, N1, Dv)
+        if out_flat.data_ptr() % 16:
+            out_user, out_flat = out_flat, torch.empty_like(out_flat)
     if lse_out is None:
         lse_flat = torch.empty((T, N1), dtype=torch.float32, device=dev)
     else:
         lse_flat = lse_out.view(T, N1)
-    q_c = q_flat.contiguous()
+    q_c = _dense16(q_flat)
     stream = torch.cuda.current_stream(dev).cuda_stream
     rc = lib.sas_forward(
         _lib.ctypes.byref(args),
@@ -258,6 +269,9 @@ def sparse_attn_sharedkv(
         stream,
     )
     _lib.check(rc, "sas_forward")
+    if out_user is not None:
+        out_user.copy_(out_flat)
+        out_flat = out_user
     if check_status:
         st = _lib.ctypes.c_uint32(0)
         _lib.check(lib.sas_read_status(_ptr(ws), _lib.ctypes.byref(st), stream), "sas_read_status")

@@ -145,6 +145,23 @@ static int check_inputs(const SasFwdArgs &a, const void *ori_kv, const int32_t *
     return SAS_OK;
 }
 
+// The kernels move rows of q, the pools, out and the workspace in 16-byte vectors (and the
+// tensor-core kernel reads q and the pools through TMA tensor maps); int32 and fp32 arrays are read
+// and written per element.  A misaligned pointer is an argument error, not a device fault.
+static bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+static int check_alignment(const void *q, const void *ori_kv, const int32_t *ori_bt, const void *cmp_kv,
+                           const int32_t *cmp_bt, const int32_t *idx, const int32_t *q_prefix, const int32_t *act_q,
+                           const int32_t *act_kv, const float *sinks, const void *out, const float *lse,
+                           const void *workspace) {
+    for (const void *p : {q, ori_kv, cmp_kv, out, workspace})
+        if (!aligned(p, 16)) return SAS_ERR_INVALID_ARG;
+    for (const void *p : {(const void *)ori_bt, (const void *)cmp_bt, (const void *)idx, (const void *)q_prefix,
+                          (const void *)act_q, (const void *)act_kv, (const void *)sinks, (const void *)lse})
+        if (!aligned(p, 4)) return SAS_ERR_INVALID_ARG;
+    return SAS_OK;
+}
+
 int sas_forward(const SasFwdArgs *args, const void *q, const void *ori_kv, const int32_t *ori_block_table,
                 const void *cmp_kv, const int32_t *cmp_block_table, const int32_t *cmp_indices,
                 const int32_t *q_prefix, const int32_t *act_q_len, const int32_t *act_kv_len, const float *sinks,
@@ -161,6 +178,9 @@ int sas_forward(const SasFwdArgs *args, const void *q, const void *ori_kv, const
     if (a.num_tokens > 0 && (!q || !out || !sinks)) return SAS_ERR_INVALID_ARG;
     const sas::FwdLayout L = fwd_layout(a);
     if (!workspace || workspace_bytes < L.total) return SAS_ERR_WORKSPACE;
+    rc = check_alignment(q, ori_kv, ori_block_table, cmp_kv, cmp_block_table, cmp_indices, q_prefix, act_q_len,
+                         act_kv_len, sinks, out, lse, workspace);
+    if (rc) return rc;
     char *ws = static_cast<char *>(workspace);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     rc = launch_prep(a, L, ws, cmp_block_table, cmp_indices, q_prefix, act_q_len, act_kv_len, s);
@@ -193,6 +213,9 @@ int sas_resolve_rows(const SasFwdArgs *args, const int32_t *ori_block_table, con
     const sas::FwdLayout L = fwd_layout(a);
     if (!workspace || workspace_bytes < L.total) return SAS_ERR_WORKSPACE;
     if (a.num_tokens > 0 && !token_info) return SAS_ERR_INVALID_ARG;
+    rc = check_alignment(nullptr, nullptr, ori_block_table, nullptr, cmp_block_table, cmp_indices, q_prefix,
+                         act_q_len, act_kv_len, nullptr, nullptr, nullptr, workspace);
+    if (rc || !aligned(token_info, 4) || !aligned(cmp_rows, 4)) return SAS_ERR_INVALID_ARG;
     char *ws = static_cast<char *>(workspace);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     rc = launch_prep(a, L, ws, cmp_block_table, cmp_indices, q_prefix, act_q_len, act_kv_len, s);

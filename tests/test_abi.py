@@ -114,6 +114,25 @@ def test_forward_rejects_before_touching_the_device(lib):
     assert lib.sas_forward(None, *([None] * 13), None, 0, None) == _lib.SAS_ERR_INVALID_ARG
 
 
+def test_forward_rejects_misaligned_pointers(lib):
+    # q, the pools, out and the workspace need 16-byte alignment (vector accesses, TMA tensor maps);
+    # the int32 / fp32 arrays 4-byte.  The check runs before any device work, so fake addresses do.
+    a = good_args()
+    base = [0x10000 * (i + 1) for i in range(16)]  # q .. lse, all 256-byte aligned
+    names = ["q", "ori_kv", "ori_bt", "cmp_kv", "cmp_bt", "idx", "q_prefix", "act_q", "act_kv", "sinks",
+             "metadata", "out", "lse"]
+    wide = {"q", "ori_kv", "cmp_kv", "out"}
+    for i, name in enumerate(names):
+        if name == "metadata":
+            continue  # not read by the kernels
+        ptrs = list(base[:13])
+        ptrs[i] += 8 if name in wide else 2
+        rc = lib.sas_forward(ctypes.byref(a), *ptrs, 0x1000000, 1 << 30, None)
+        assert rc == _lib.SAS_ERR_INVALID_ARG, name
+    rc = lib.sas_forward(ctypes.byref(a), *base[:13], 0x1000008, 1 << 30, None)
+    assert rc == _lib.SAS_ERR_INVALID_ARG, "workspace"
+
+
 def test_cu_seqlens_flag(lib):
     # act_q_len may be NULL only with SAS_FWD_FLAG_CU_SEQLENS; unknown flag bits are rejected
     a = good_args()

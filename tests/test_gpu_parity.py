@@ -375,3 +375,28 @@ def test_rows_outside_every_request_are_zero(api, cuda_device, kernel):
     np.testing.assert_array_equal(out_t[:T], ref_out)
     np.testing.assert_array_equal(lse_t[:T], ref_lse)
     assert not out_t[T:].any() and not lse_t[T:].any()
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_misaligned_views_are_rehomed(api, cuda_device, kernel):
+    """q and out views that start one element into an allocation (not 16-byte aligned) give the
+    same bits as aligned tensors: the API copies q, and writes out through an aligned buffer."""
+    if kernel == "tc" and not tc_available():
+        pytest.skip("tensor-core path not built")
+    from dsv4_planb_b200 import workloads as W
+
+    dev = cuda_device
+    wl = W.make_workload(name="misaligned", q_lens=[1, 2], kv_lens=[900, 3000], num_heads=128, topk=256, seed=9)
+    ref_out, ref_lse = run(api, wl, kernel, dev)
+    kw = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in wl.api_kwargs().items()}
+    q = wl.q.to(dev)
+    qv = torch.empty(q.numel() + 1, dtype=q.dtype, device=dev)[1:].view(q.shape)
+    qv.copy_(q)
+    T, N1 = q.shape[0], q.shape[1]
+    ov = torch.empty(T * N1 * wl.v_head_dim + 1, dtype=q.dtype, device=dev)[1:].view(T, N1, wl.v_head_dim)
+    assert qv.data_ptr() % 16 and ov.data_ptr() % 16
+    out, lse = api.sparse_attn_sharedkv(qv, return_softmax_lse=True, kernel=kernel, check_status=True, out=ov, **kw)
+    torch.cuda.synchronize()
+    assert out.data_ptr() == ov.data_ptr()
+    np.testing.assert_array_equal(out.float().cpu().numpy(), ref_out)
+    np.testing.assert_array_equal(lse.cpu().numpy(), ref_lse)
