@@ -1012,8 +1012,9 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// Row-gather tensor map over a paged pool viewed as [rows, D] (box: 64 columns x 1 row, 128-byte
-// swizzle).  Row `rows` (one past the end) lies outside the map and reads as zeros.
+// Tensor map over a [rows, D] array with 128-byte swizzle and boxes of 64 columns x `box_rows` rows.
+// Pools (box_rows 1, for tile::gather4): row `rows` (one past the end) lies outside the map and
+// reads as zeros.  q (box_rows 64, rows = T * N1): a box that runs past the last row reads zeros.
 int make_map(CUtensorMap *map, const void *base, int64_t rows, int D, bool bf16, uint32_t box_rows = 1) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return SAS_ERR_CUDA;

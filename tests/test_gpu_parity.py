@@ -400,3 +400,27 @@ def test_misaligned_views_are_rehomed(api, cuda_device, kernel):
     assert out.data_ptr() == ov.data_ptr()
     np.testing.assert_array_equal(out.float().cpu().numpy(), ref_out)
     np.testing.assert_array_equal(lse.cpu().numpy(), ref_lse)
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+@pytest.mark.parametrize("heads,q_lens", [(16, [1]), (100, [1, 2])])
+def test_head_counts_off_the_q_box(api, cuda_device, kernel, heads, q_lens):
+    """Head counts that are not a multiple of the 64-row Q box: with 16 heads and one token the
+    box is taller than all of q (rows past the end read zeros); with 100 heads a token's second
+    box reaches into the next token's rows (heads past N1 are computed and dropped)."""
+    if kernel == "tc" and not tc_available():
+        pytest.skip("tensor-core path not built")
+    from dsv4_planb_b200 import workloads as W
+
+    wl = W.make_workload(name="heads", q_lens=q_lens, kv_lens=[2500 + 1000 * i for i in range(len(q_lens))],
+                         num_heads=heads, topk=512, seed=13)
+    out, lse = run(api, wl, kernel, cuda_device)
+    wl_c = wl.to("cpu")
+    sample = list(range(sum(q_lens)))
+    ref_out, ref_lse, _ = O.sparse_attn_sharedkv_oracle(
+        wl_c.q, ori_kv=wl_c.ori_kv, ori_block_table=wl_c.ori_block_table, seqused_kv=wl_c.seqused_kv,
+        q_prefix=wl_c.cu_seqlens_q[:-1], act_q=wl_c.cu_seqlens_q[1:] - wl_c.cu_seqlens_q[:-1], sinks=wl_c.sinks,
+        softmax_scale=wl_c.softmax_scale, cmp_kv=wl_c.cmp_kv, cmp_block_table=wl_c.cmp_block_table,
+        cmp_sparse_indices=wl_c.cmp_sparse_indices, cmp_ratio=wl_c.cmp_ratio, v_head_dim=wl_c.v_head_dim,
+        tokens=sample)
+    assert_close_to_golden(out[sample], lse[sample], ref_out[sample], ref_lse[sample], f"{kernel} h{heads}")
