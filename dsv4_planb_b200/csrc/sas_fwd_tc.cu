@@ -86,14 +86,19 @@ constexpr int kQStages = 2;
 constexpr int kQChunksPerStage = kQTmaChunks / kQStages;
 constexpr uint32_t kQStageBytes = 2 * kQChunksPerStage * kChunkBytes;  // 64 KiB: eight 64x64 boxes
 static_assert(kKStages > kQStages, "a K tile must fit beside the Q stages");
-// Exception: a cluster's first unit of kQRegMinTiles tiles or more loads all of Q through the
-// softmax warps' registers.  At the start the gather of K bounds such a unit, and the register
-// path (nine round trips, off the TMA unit) hides behind three stages of K, where the TMA path
-// would hold two of them.  Later units' Q by TMA overlaps the previous unit's last tiles.
-// Measured, kernel time, first unit by registers / by TMA: one 34-tile token a cluster (c2)
-// 98.8 / 101.1 us; decode pieces of 9 tiles (B=16) 49.0 / 47.2 us.  The threshold sits between.
+// Exception: a cluster's first unit of kQRegMinTiles tiles or more takes only kQFirstStages stage
+// (chunks 0-3 by TMA) and loads chunks 4-8 through the softmax warps' registers.  At the start the
+// gather of K bounds such a unit: two stages of Q would hold back the second and third K tiles,
+// while a register load (a round trip per chunk, off the TMA unit) overlaps them.  Later units'
+// Q overlaps the previous unit's last tiles and takes the two stages.  Measured, kernel time,
+// first unit with 0 / 1 / 2 TMA stages: one 34-tile token a cluster (c2) 98.9 / 96.3 / 101.1 us;
+// decode pieces of 9 tiles (B=16) 49.0 / - / 47.2 us.  The threshold sits between.
 constexpr int kQRegMinTiles = 20;
-__device__ __forceinline__ bool q_by_tma(int tiles, bool first) { return !first || tiles < kQRegMinTiles; }
+constexpr int kQFirstStages = 1;
+// Ring stages a unit's Q takes (chunks [0, 4 x stages) by TMA, the rest by registers).
+__device__ __forceinline__ int q_stages(int tiles, bool first) {
+    return !first || tiles < kQRegMinTiles ? kQStages : kQFirstStages;
+}
 
 // Unit queue: the score CTA's producer warp 4 takes unit ids from a global counter (the next one
 // fetched while the current one runs) and publishes them to every role of both CTAs through a
@@ -365,13 +370,13 @@ __device__ void producer(const TcArgs &p, const Sync &sy, const CUtensorMap *ori
         if (it.skip) continue;
         const int32_t *crow = p.rows + (int64_t)it.t * p.row_cap;
         int32_t fetched = pt < kBK && it.j1 > it.j0 ? key_fetch(p, it, crow, it.j0, pt) : -1;
-        const bool q_tma = q_by_tma(it.j1 - it.j0, first);
+        const int q_st = q_stages(it.j1 - it.j0, first);
         if (it.j1 > it.j0) first = false;
-        if (q_map != nullptr && it.j1 > it.j0 && q_tma) {
-            // score CTA: the unit's Q, dims [0, 512), into the next two stages (slab 2i + half of
-            // a stage = chunk i of the stage, heads 64 half .. 64 half + 63; rows past the last
-            // token read zeros)
-            for (int r = 0; r < kQStages; ++r) {
+        if (q_map != nullptr && it.j1 > it.j0) {
+            // score CTA: the unit's Q, dims [0, 256 q_st), into the next q_st stages (slab 2i +
+            // half of a stage = chunk i of the stage, heads 64 half .. 64 half + 63; rows past the
+            // last token read zeros)
+            for (int r = 0; r < q_st; ++r) {
                 const int st = cnt % stages;
                 const uint32_t fb = smem_u32(&full[st]);
                 const bool ok = wait_warp(sy, smem_u32(&empty[st]), ((cnt / stages) & 1) ^ 1);
@@ -541,29 +546,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (t < 0) break;
                 const Item it = load_unit<kSplit>(p, t);
                 if (it.skip || it.ntiles == 0) continue;
-                const bool q_tma = q_by_tma(it.j1 - it.j0, first);
+                const int q_st = q_stages(it.j1 - it.j0, first);
                 first = false;
-                // Q dims [0, 512) from the two stages the producer filled -> TMEM columns [0, 256).
+                // Q dims [0, 256 q_st) from the q_st stages the producer filled -> TMEM columns
+                // [0, 128 q_st).
                 // The previous unit's QK products read those columns: the copy waits for the last
                 // of them (tcgen05.cp is ordered before later MMAs, not after earlier ones).
-                if (q_tma) {
-                    for (int r = 0; r < kQStages; ++r)
+                if (q_st > 0) {
+                    for (int r = 0; r < q_st; ++r)
                         if (!wait_warp(sy, smem_u32(&hd->k_full[(kc + r) % kKStages]), ((kc + r) / kKStages) & 1))
                             goto done;
                     if (sc > 0 && !wait_warp(sy, smem_u32(&hd->s_full[(sc - 1) & 1]), ((sc - 1) >> 1) & 1)) goto done;
                     tc_fence_after();
                     if (lane == 0) {
-                        for (int r = 0; r < kQStages; ++r) {
+                        for (int r = 0; r < q_st; ++r) {
                             const uint32_t qb = smem_u32(kbuf + (size_t)((kc + r) % kKStages) * kstage);
                             for (int i = 0; i < kQChunksPerStage; ++i)
                                 for (int kq = 0; kq < 4; ++kq)
                                     tmem_cp_128x256b(tmem + ((kQChunksPerStage * r + i) * 4 + kq) * 8,
                                                      sdesc_sw128(qb + 2 * i * kChunkBytes + kq * 32, 16, 1024));
                         }
-                        for (int r = 0; r < kQStages; ++r) tc_commit(smem_u32(&hd->k_empty[(kc + r) % kKStages]));
+                        for (int r = 0; r < q_st; ++r) tc_commit(smem_u32(&hd->k_empty[(kc + r) % kKStages]));
                     }
                     __syncwarp();
-                    kc += kQStages;
+                    kc += q_st;
                 }
                 if (!wait_warp(sy, smem_u32(&hd->q_full), qc & 1)) goto done;
                 ++qc;
@@ -605,15 +611,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (p.lse && h < p.N1) p.lse[(int64_t)t * p.N1 + h] = it.valid ? p.sinks[h] : 0.f;
                     continue;
                 }
-                // ---- Q row h -> TMEM (A operand: 2 elements per 32-bit column): dims [512, D_qk),
-                // or all of them for a long first unit; dims [0, 512) otherwise come through the K
-                // ring and tcgen05.cp
+                // ---- Q row h -> TMEM (A operand: 2 elements per 32-bit column): dims
+                // [256 q_st, D_qk); dims [0, 256 q_st) come through the K ring and tcgen05.cp
                 {
-                    const bool q_tma = q_by_tma(it.j1 - it.j0, first);
+                    const int q_st = q_stages(it.j1 - it.j0, first);
                     first = false;
                     const uint4 *qrow = reinterpret_cast<const uint4 *>(
                         reinterpret_cast<const uint16_t *>(p.q) + ((int64_t)t * p.N1 + (h < p.N1 ? h : 0)) * p.Dq);
-                    for (int c = q_tma ? kQTmaChunks : 0; c < qch; ++c) {
+                    for (int c = kQChunksPerStage * q_st; c < qch; ++c) {
                         uint32_t r[32];
 #pragma unroll
                         for (int v = 0; v < 8; ++v) {
