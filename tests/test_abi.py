@@ -208,3 +208,21 @@ def test_strerror_and_version(lib):
     assert lib.sas_abi_version() == 1
     for rc in range(6):
         assert _lib.strerror(rc)
+
+
+def test_api_rehomes_views_that_start_inside_a_vector():
+    # The Python layer hands the C ABI only 16-byte aligned q / pool bases: a view at an odd element
+    # offset is copied (same values), an aligned one passes through untouched.
+    import torch
+
+    from dsv4_planb_b200.api import _dense16
+
+    base = torch.arange(64, dtype=torch.bfloat16)
+    aligned = base[8:40].view(4, 8)  # 16 bytes into a (>= 16-byte aligned) allocation
+    assert _dense16(aligned).data_ptr() == aligned.data_ptr()
+    odd = base[1:33].view(4, 8)
+    fixed = _dense16(odd)
+    assert fixed.data_ptr() % 16 == 0 and fixed.data_ptr() != odd.data_ptr()
+    assert torch.equal(fixed, odd)
+    strided = base.view(8, 8)[:, :4]  # non-contiguous: made dense
+    assert _dense16(strided).is_contiguous() and torch.equal(_dense16(strided), strided)
