@@ -45,6 +45,10 @@ int scratch_for_current_device(char **out) {
     return SAS_OK;
 }
 
+// The same pointer rule as sas_forward: 16-byte vectors and TMA tensor maps over q, the pools and
+// out; per-element access to the int32 and fp32 arrays.  A misaligned pointer is an argument error.
+bool misaligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) != 0; }
+
 } // namespace
 
 extern "C" int sas_forward_noalloc(const SasFwdArgs *args, const void *q, const void *ori_kv,
@@ -65,6 +69,12 @@ extern "C" int sas_forward_noalloc(const SasFwdArgs *args, const void *q, const 
     if (a.num_tokens > 0 && (!q || !out || !sinks)) return SAS_ERR_INVALID_ARG;
     const sas::FwdLayout L = sas_host::fwd_layout(a);
     if (L.total > (size_t)SAS_NOALLOC_SCRATCH_BYTES) return SAS_ERR_WORKSPACE;
+    for (const void *p : {q, ori_kv, cmp_kv, (const void *)out})
+        if (misaligned(p, 16)) return SAS_ERR_INVALID_ARG;
+    for (const void *p : {(const void *)ori_block_table, (const void *)cmp_block_table, (const void *)cmp_indices,
+                          (const void *)q_prefix, (const void *)act_q_len, (const void *)act_kv_len,
+                          (const void *)sinks, (const void *)lse})
+        if (misaligned(p, 4)) return SAS_ERR_INVALID_ARG;
     char *ws = nullptr;
     if ((rc = scratch_for_current_device(&ws))) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);

@@ -133,6 +133,16 @@ def test_forward_rejects_misaligned_pointers(lib):
     assert rc == _lib.SAS_ERR_INVALID_ARG, "workspace"
 
 
+def test_noalloc_rejects_misaligned_pointers(lib):
+    # the entry point without a workspace follows the same pointer rule, checked before any device work
+    a = good_args()
+    base = [0x10000 * (i + 1) for i in range(13)]
+    for i, wide in [(0, True), (1, True), (3, True), (11, True), (2, False), (9, False), (12, False)]:
+        ptrs = list(base)
+        ptrs[i] += 8 if wide else 2
+        assert lib.sas_forward_noalloc(ctypes.byref(a), *ptrs, None) == _lib.SAS_ERR_INVALID_ARG, i
+
+
 def test_cu_seqlens_flag(lib):
     # act_q_len may be NULL only with SAS_FWD_FLAG_CU_SEQLENS; unknown flag bits are rejected
     a = good_args()
