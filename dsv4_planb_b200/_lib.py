@@ -43,6 +43,7 @@ EXPORTS = (
     "sas_forward_kernel_count",
     "sas_forward",
     "sas_forward_noalloc",
+    "sas_noalloc_read_status",
     "sas_resolve_rows",
     "sas_read_status",
     "sas_set_kernel_events",
@@ -122,6 +123,7 @@ _SIGNATURES = {
     "sas_forward_kernel_count": (ctypes.c_int, [ctypes.POINTER(SasFwdArgs), ctypes.POINTER(ctypes.c_int32)]),
     "sas_forward": (ctypes.c_int, [ctypes.POINTER(SasFwdArgs)] + [_P] * 13 + [_P, _SZ, _P]),
     "sas_forward_noalloc": (ctypes.c_int, [ctypes.POINTER(SasFwdArgs)] + [_P] * 13 + [_P]),
+    "sas_noalloc_read_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), _P]),
     "sas_resolve_rows": (ctypes.c_int, [ctypes.POINTER(SasFwdArgs)] + [_P] * 8 + [_P, _SZ, _P]),
     "sas_read_status": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_uint32), _P]),
     "sas_set_kernel_events": (ctypes.c_int, [_P, _P]),

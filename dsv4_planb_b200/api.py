@@ -7,6 +7,12 @@ api.py:196-202), the same TND / BSND handling (api.py:204-240), the same
 assertions (api.py:186-191, 247-249, 362-364) and the same return value
 (``out``, or ``(out, lse)`` when ``return_softmax_lse``, api.py:388-397).
 
+The launch itself is a registered torch operator, ``torch.ops.sas_b200.sparse_attn_sharedkv``
+(outputs allocated by the op) and ``torch.ops.sas_b200.sparse_attn_sharedkv_out`` (writes
+caller-owned ``out`` / ``lse``), each with a fake (meta) implementation: the dispatcher, fake
+tensors, ``torch.compile(fullgraph=True)`` and CUDA-graph capture see one opaque op, where the
+reference calls its JIT kernel directly (api.py:372-384).
+
 Differences, all widenings of the reference contract:
 
 * any head count N1 and any ``D_qk % 8 == 0`` (the reference pins N1 = 64,
@@ -15,14 +21,18 @@ Differences, all widenings of the reference contract:
 * ``metadata`` is accepted and checked for size but not needed: the B200
   kernels plan their own work split over 148 SMs (no scheduler call and no
   host sync when it is omitted); ``core_num`` is accepted and ignored;
+* no host synchronisation: scenario 2 (CFA) takes each token's compressed range
+  from the block table on the device (the reference reads ``seqused_kv.max()``
+  on the host, api.py:260), and TND needs none once ``max_seqlen_q`` is given;
 * extra keywords ``kernel`` ("auto" | "simt" | "tc"), ``max_seqlen_q`` (skips
   the host read of ``cu_seqlens_q``), ``out`` / ``lse_out`` (preallocated
-  outputs) and ``check_status`` (read the device status word, synchronising).
+  outputs), ``check_status`` (read the device status word, synchronising) and
+  ``split_tiles``.
 """
 
 from __future__ import annotations
 
-from typing import Optional, Tuple, Union
+from typing import List, Optional, Tuple, Union
 
 import torch
 
@@ -30,7 +40,6 @@ from . import _lib
 
 SAS_META_SIZE = 1024
 DEFAULT_CORE_NUM = 24
-
 
 def _dtype_code(t: torch.dtype) -> int:
     if t == torch.bfloat16:
@@ -47,9 +56,20 @@ def _i32(t: torch.Tensor, device) -> torch.Tensor:
 def _dense16(t: torch.Tensor) -> torch.Tensor:
     """Contiguous, with a 16-byte aligned base: the kernels move rows in 16-byte vectors and the
     tensor-core kernel reads q and the pools through TMA tensor maps.  A view that starts inside a
-    vector (an odd element offset) is copied; the C ABI rejects such a pointer."""
+    vector (an odd element offset) is copied; the C ABI rejects such a pointer.  For per-call
+    tensors (q); the KV pools go through _pool16."""
     t = t.contiguous()
     return t if t.data_ptr() % 16 == 0 else t.clone()
+
+
+def _pool16(t: torch.Tensor, name: str) -> torch.Tensor:
+    """A paged KV pool must already be dense with a 16-byte aligned base: copying a pool (which can
+    be gigabytes) on every call to re-home it would hide a large cost behind a slow step."""
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous (a paged KV pool is not copied per call)")
+    if t.data_ptr() % 16:
+        raise ValueError(f"{name} must start on a 16-byte boundary (a paged KV pool is not copied per call)")
+    return t
 
 
 def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
@@ -59,6 +79,193 @@ def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
 def _workspace(nbytes: int, device) -> torch.Tensor:
     # The caching allocator makes this cheap and keeps it stream-ordered.
     return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+def _scenario(cmp_kv, cmp_sparse_indices) -> int:
+    if cmp_kv is None:
+        return 1
+    return 2 if cmp_sparse_indices is None else 3
+
+
+def _out_shapes(q: torch.Tensor, layout_q: str, v_head_dim: int):
+    if layout_q == "TND":
+        T, N1, _ = q.shape
+        return (T, N1, v_head_dim), (T, N1)
+    B, S, N1, _ = q.shape
+    return (B, S, N1, v_head_dim), (B, S, N1)
+
+
+def _launch(q, ori_kv, cmp_kv, cmp_sparse_indices, ori_block_table, cmp_block_table, cu_seqlens_q, seqused_kv,
+            sinks, metadata, softmax_scale, cmp_ratio, ori_win_left, layout_q, v_head_dim, kernel, max_seqlen_q,
+            split_tiles, check_status, out, lse_out):
+    """Marshal one sas_forward call (the body of both registered ops).  ``out`` / ``lse_out`` are the
+    outputs in the layout of ``q``; ``max_seqlen_q`` < 0 reads it from ``cu_seqlens_q`` (host sync)."""
+    dev = q.device
+    scenario = _scenario(cmp_kv, cmp_sparse_indices)
+    if layout_q == "TND":
+        T, N1, D = q.shape
+        q_flat = q
+        cu = _i32(cu_seqlens_q, dev)
+        B = cu.numel() - 1
+        q_prefix = cu  # with SAS_FWD_FLAG_CU_SEQLENS the kernels derive act_q = cu[b+1] - cu[b]
+        act_q = None
+        if max_seqlen_q < 0:
+            cu_h = cu_seqlens_q.detach().to("cpu", torch.int64)
+            max_seqlen_q = int((cu_h[1:] - cu_h[:-1]).max().item()) if B > 0 else 0
+        idx_flat = _i32(cmp_sparse_indices, dev) if scenario == 3 else None
+    else:
+        B, S_max, N1, D = q.shape
+        T = B * S_max
+        q_flat = q.reshape(T, N1, D)
+        q_prefix = torch.arange(B, dtype=torch.int32, device=dev) * S_max
+        if cu_seqlens_q is not None:
+            cu = _i32(cu_seqlens_q, dev)
+            act_q = (cu[1:] - cu[:-1]).contiguous()
+        else:
+            act_q = torch.full((B,), S_max, dtype=torch.int32, device=dev)
+        max_seqlen_q = S_max if max_seqlen_q < 0 else max_seqlen_q
+        if scenario == 3:
+            ci = cmp_sparse_indices
+            idx_flat = _i32(ci.reshape(T, ci.shape[2], ci.shape[3]), dev)
+        else:
+            idx_flat = None
+    seq_kv = _i32(seqused_kv, dev)
+    if scenario == 3:
+        N2 = idx_flat.shape[1]
+        K = idx_flat.shape[2]
+    else:
+        N2 = (cmp_kv if scenario == 2 else ori_kv).shape[2]
+        K = 0
+    if N2 != 1:
+        raise ValueError(f"only one KV head is supported (got N2={N2})")
+    Dv = v_head_dim
+    ori_kv_d = _pool16(ori_kv, "ori_kv")
+    ori_bt = _i32(ori_block_table, dev)
+    if ori_bt.dim() != 2 or ori_bt.shape[0] < B:
+        raise ValueError(f"ori_block_table must be [B>={B}, table_len] (got {tuple(ori_bt.shape)})")
+    if cmp_block_table is not None and (cmp_block_table.dim() != 2 or cmp_block_table.shape[0] < B):
+        raise ValueError(f"cmp_block_table must be [B>={B}, table_len] (got {tuple(cmp_block_table.shape)})")
+    if idx_flat is not None and (idx_flat.dim() != 3 or idx_flat.shape[0] != T):
+        raise ValueError(f"cmp_sparse_indices must hold one row per query token (got {tuple(idx_flat.shape)})")
+    if scenario >= 2:
+        cmp_kv_d = _pool16(cmp_kv, "cmp_kv")
+        cmp_bt = _i32(cmp_block_table, dev)
+    else:
+        cmp_kv_d = cmp_bt = None
+    sinks_d = sinks.to(device=dev, dtype=torch.float32).contiguous()
+    if metadata is not None:
+        metadata = _i32(metadata.reshape(SAS_META_SIZE), dev)
+
+    args = _lib.SasFwdArgs()
+    args.batch = B
+    args.num_tokens = T
+    args.max_q_len = int(max_seqlen_q)
+    args.num_heads = N1
+    args.num_kv_heads = N2
+    args.head_dim = D
+    args.v_head_dim = Dv
+    args.ori_block_num, args.ori_block_size = ori_kv_d.shape[0], ori_kv_d.shape[1]
+    args.ori_table_len = ori_bt.shape[1]
+    if scenario >= 2:
+        args.cmp_block_num, args.cmp_block_size = cmp_kv_d.shape[0], cmp_kv_d.shape[1]
+        args.cmp_table_len = cmp_bt.shape[1]
+    args.topk = K
+    args.cmp_ratio = int(cmp_ratio)
+    args.scenario = scenario
+    args.max_cmp_len = 0  # the kernels resolve CFA's dense range through the table
+    args.ori_win_left = ori_win_left
+    args.ori_win_right = 0
+    args.ori_mask_mode = 4
+    args.cmp_mask_mode = 3
+    args.dtype = _dtype_code(q.dtype)
+    args.softmax_scale = float(softmax_scale)
+    args.kernel = _lib.KERNELS[kernel]
+    args.flags = _lib.SAS_FWD_FLAG_CU_SEQLENS if layout_q == "TND" else 0
+    args.split_tiles = int(split_tiles)
+
+    lib = _lib.load()
+    nbytes = _lib.ctypes.c_size_t(0)
+    _lib.check(lib.sas_workspace_size(_lib.ctypes.byref(args), _lib.ctypes.byref(nbytes)), "sas_workspace_size")
+    ws = _workspace(nbytes.value, dev)
+    out_flat = out.view(T, N1, Dv)
+    out_user = None  # a caller's out that starts inside a 16-byte vector: written through a copy
+    if out_flat.data_ptr() % 16:
+        out_user, out_flat = out_flat, torch.empty_like(out_flat)
+    lse_flat = lse_out.view(T, N1)
+    q_c = _dense16(q_flat)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    rc = lib.sas_forward(
+        _lib.ctypes.byref(args),
+        _ptr(q_c),
+        _ptr(ori_kv_d),
+        _ptr(ori_bt),
+        _ptr(cmp_kv_d),
+        _ptr(cmp_bt),
+        _ptr(idx_flat),
+        _ptr(q_prefix),
+        _ptr(act_q),
+        _ptr(seq_kv),
+        _ptr(sinks_d),
+        _ptr(metadata),
+        _ptr(out_flat),
+        _ptr(lse_flat),
+        _ptr(ws),
+        ws.numel(),
+        stream,
+    )
+    _lib.check(rc, "sas_forward")
+    if out_user is not None:
+        out_user.copy_(out_flat)
+    if check_status:
+        st = _lib.ctypes.c_uint32(0)
+        _lib.check(lib.sas_read_status(_ptr(ws), _lib.ctypes.byref(st), stream), "sas_read_status")
+        if st.value:
+            raise RuntimeError(f"sas_forward device status: {_lib.status_names(st.value)}")
+
+
+@torch.library.custom_op("sas_b200::sparse_attn_sharedkv", mutates_args=(), device_types="cuda")
+def _op(q: torch.Tensor, ori_kv: torch.Tensor, cmp_kv: Optional[torch.Tensor],
+        cmp_sparse_indices: Optional[torch.Tensor], ori_block_table: torch.Tensor,
+        cmp_block_table: Optional[torch.Tensor], cu_seqlens_q: Optional[torch.Tensor], seqused_kv: torch.Tensor,
+        sinks: torch.Tensor, metadata: Optional[torch.Tensor], softmax_scale: float, cmp_ratio: int,
+        ori_win_left: int, layout_q: str, v_head_dim: int, kernel: str, max_seqlen_q: int, split_tiles: int,
+        check_status: bool) -> Tuple[torch.Tensor, torch.Tensor]:
+    """sparse_attn_sharedkv with op-owned outputs: returns ``(out, lse)`` in the layout of ``q``."""
+    o_shape, l_shape = _out_shapes(q, layout_q, v_head_dim)
+    out = torch.empty(o_shape, dtype=q.dtype, device=q.device)
+    lse = torch.empty(l_shape, dtype=torch.float32, device=q.device)
+    _launch(q, ori_kv, cmp_kv, cmp_sparse_indices, ori_block_table, cmp_block_table, cu_seqlens_q, seqused_kv,
+            sinks, metadata, softmax_scale, cmp_ratio, ori_win_left, layout_q, v_head_dim, kernel, max_seqlen_q,
+            split_tiles, check_status, out, lse)
+    return out, lse
+
+
+@_op.register_fake
+def _op_fake(q, ori_kv, cmp_kv, cmp_sparse_indices, ori_block_table, cmp_block_table, cu_seqlens_q, seqused_kv,
+             sinks, metadata, softmax_scale, cmp_ratio, ori_win_left, layout_q, v_head_dim, kernel, max_seqlen_q,
+             split_tiles, check_status):
+    o_shape, l_shape = _out_shapes(q, layout_q, v_head_dim)
+    return q.new_empty(o_shape), q.new_empty(l_shape, dtype=torch.float32)
+
+
+@torch.library.custom_op("sas_b200::sparse_attn_sharedkv_out", mutates_args=("out", "lse"), device_types="cuda")
+def _op_out(q: torch.Tensor, ori_kv: torch.Tensor, cmp_kv: Optional[torch.Tensor],
+            cmp_sparse_indices: Optional[torch.Tensor], ori_block_table: torch.Tensor,
+            cmp_block_table: Optional[torch.Tensor], cu_seqlens_q: Optional[torch.Tensor], seqused_kv: torch.Tensor,
+            sinks: torch.Tensor, metadata: Optional[torch.Tensor], softmax_scale: float, cmp_ratio: int,
+            ori_win_left: int, layout_q: str, v_head_dim: int, kernel: str, max_seqlen_q: int, split_tiles: int,
+            check_status: bool, out: torch.Tensor, lse: torch.Tensor) -> None:
+    """sparse_attn_sharedkv into caller-owned ``out`` / ``lse`` (layout of ``q``)."""
+    _launch(q, ori_kv, cmp_kv, cmp_sparse_indices, ori_block_table, cmp_block_table, cu_seqlens_q, seqused_kv,
+            sinks, metadata, softmax_scale, cmp_ratio, ori_win_left, layout_q, v_head_dim, kernel, max_seqlen_q,
+            split_tiles, check_status, out, lse)
+
+
+@_op_out.register_fake
+def _op_out_fake(q, ori_kv, cmp_kv, cmp_sparse_indices, ori_block_table, cmp_block_table, cu_seqlens_q, seqused_kv,
+                 sinks, metadata, softmax_scale, cmp_ratio, ori_win_left, layout_q, v_head_dim, kernel, max_seqlen_q,
+                 split_tiles, check_status, out, lse):
+    return None
 
 
 def sparse_attn_sharedkv(
@@ -106,6 +313,8 @@ def sparse_attn_sharedkv(
     (caller-owned outputs), ``check_status`` (raise on device-side status bits) and
     ``split_tiles`` (piece size, in 64-key tiles, for cutting long tokens across the
     tensor-core path's clusters; 0 lets the library decide; see ``sharding.split_hint``).
+    Everything here is shape logic that ``torch.compile`` traces; the launch is the
+    registered op ``torch.ops.sas_b200.sparse_attn_sharedkv`` (``..._out`` with ``out``).
     """
     del seqused_q, core_num  # API parity (the reference kernel does not read them either)
     assert ori_mask_mode == 4, "only ori_mask_mode=4 supported"
@@ -117,172 +326,39 @@ def sparse_attn_sharedkv(
         raise ValueError(f"kernel must be one of {sorted(_lib.KERNELS)}")
     if not q.is_cuda:
         raise ValueError("q must be a CUDA tensor (sas_b200 has no CPU path)")
-    dev = q.device
-    dtype_code = _dtype_code(q.dtype)
-
-    if cmp_kv is None:
-        scenario = 1
-    elif cmp_sparse_indices is None:
-        scenario = 2
-    else:
-        scenario = 3
-
-    # ---- flat [T, ...] view and per-request query ranges (api.py:204-240)
+    scenario = _scenario(cmp_kv, cmp_sparse_indices)
     if layout_q == "TND":
         assert cu_seqlens_q is not None, "cu_seqlens_q is required for TND"
-        T, N1, D = q.shape
-        q_flat = q
-        cu = _i32(cu_seqlens_q, dev)
-        B = cu.numel() - 1
-        q_prefix = cu  # with SAS_FWD_FLAG_CU_SEQLENS the kernels derive act_q = cu[b+1] - cu[b]
-        act_q = None
-        if max_seqlen_q is None:
-            cu_h = cu_seqlens_q.detach().to("cpu", torch.int64)
-            max_seqlen_q = int((cu_h[1:] - cu_h[:-1]).max().item()) if B > 0 else 0
-        idx_flat = _i32(cmp_sparse_indices, dev) if scenario == 3 else None
-    else:
-        B, S_max, N1, D = q.shape
-        T = B * S_max
-        q_flat = q.reshape(T, N1, D)
-        q_prefix = torch.arange(B, dtype=torch.int32, device=dev) * S_max
-        if cu_seqlens_q is not None:
-            cu = _i32(cu_seqlens_q, dev)
-            act_q = (cu[1:] - cu[:-1]).contiguous()
-        else:
-            act_q = torch.full((B,), S_max, dtype=torch.int32, device=dev)
-        max_seqlen_q = S_max if max_seqlen_q is None else max_seqlen_q
-        if scenario == 3:
-            ci = cmp_sparse_indices
-            idx_flat = _i32(ci.reshape(T, ci.shape[2], ci.shape[3]), dev)
-        else:
-            idx_flat = None
-
-    seq_kv = _i32(seqused_kv, dev)
-
-    # ---- scenario-specific sizes (api.py:244-282)
-    max_cmp_len = 0
+    D = q.shape[-1]
     if scenario == 3:
-        N2 = idx_flat.shape[1]
-        K = topk_cmp if topk_cmp is not None else idx_flat.shape[2]
-        assert K == idx_flat.shape[2], "topk_cmp does not match cmp_sparse_indices last dim"
+        K = cmp_sparse_indices.shape[-1]
+        assert topk_cmp is None or topk_cmp == K, "topk_cmp does not match cmp_sparse_indices last dim"
     elif scenario == 2:
-        N2 = cmp_kv.shape[2]
-        K = 0
         assert cmp_ratio is not None, "cmp_ratio is required with cmp_kv"
-        max_cmp_len = int(seqused_kv.max().item()) // cmp_ratio if seqused_kv.numel() else 0
-    else:
-        N2 = ori_kv.shape[2]
-        K = 0
-    if N2 != 1:
-        raise ValueError(f"only one KV head is supported (got N2={N2})")
     Dv = D if v_head_dim is None else int(v_head_dim)
     if ori_kv.shape[-1] != D:
         raise ValueError(f"ori_kv row width {ori_kv.shape[-1]} != head_dim {D}")
     if ori_kv.dtype != q.dtype or (cmp_kv is not None and cmp_kv.dtype != q.dtype):
         raise ValueError("q, ori_kv and cmp_kv must share one dtype")
-
-    ori_kv_d = _dense16(ori_kv.to(dev))
-    ori_bt = _i32(ori_block_table, dev)
-    if ori_bt.dim() != 2 or ori_bt.shape[0] < B:
-        raise ValueError(f"ori_block_table must be [B>={B}, table_len] (got {tuple(ori_bt.shape)})")
-    if cmp_block_table is not None and (cmp_block_table.dim() != 2 or cmp_block_table.shape[0] < B):
-        raise ValueError(f"cmp_block_table must be [B>={B}, table_len] (got {tuple(cmp_block_table.shape)})")
-    if idx_flat is not None and (idx_flat.dim() != 3 or idx_flat.shape[0] != T):
-        raise ValueError(f"cmp_sparse_indices must hold one row per query token (got {tuple(idx_flat.shape)})")
-    if scenario >= 2:
-        cmp_kv_d = _dense16(cmp_kv.to(dev))
-        cmp_bt = _i32(cmp_block_table, dev)
-        cmp_ratio_eff = int(cmp_ratio) if cmp_ratio is not None else 4
-    else:
-        cmp_kv_d = cmp_bt = None
-        cmp_ratio_eff = int(cmp_ratio) if cmp_ratio is not None else 4
-    sinks_d = sinks.to(device=dev, dtype=torch.float32).contiguous()
     if metadata is not None:
         assert metadata.numel() == SAS_META_SIZE, (
             f"metadata must have {SAS_META_SIZE} int32 entries (got {metadata.numel()})"
         )
-        metadata = _i32(metadata.reshape(SAS_META_SIZE), dev)
-
-    args = _lib.SasFwdArgs()
-    args.batch = B
-    args.num_tokens = T
-    args.max_q_len = int(max_seqlen_q)
-    args.num_heads = N1
-    args.num_kv_heads = N2
-    args.head_dim = D
-    args.v_head_dim = Dv
-    args.ori_block_num, args.ori_block_size = ori_kv_d.shape[0], ori_kv_d.shape[1]
-    args.ori_table_len = ori_bt.shape[1]
-    if scenario >= 2:
-        args.cmp_block_num, args.cmp_block_size = cmp_kv_d.shape[0], cmp_kv_d.shape[1]
-        args.cmp_table_len = cmp_bt.shape[1]
-    args.topk = K
-    args.cmp_ratio = cmp_ratio_eff
-    args.scenario = scenario
-    args.max_cmp_len = max_cmp_len
-    args.ori_win_left = ori_win_left
-    args.ori_win_right = ori_win_right
-    args.ori_mask_mode = ori_mask_mode
-    args.cmp_mask_mode = cmp_mask_mode
-    args.dtype = dtype_code
-    args.softmax_scale = float(softmax_scale)
-    args.kernel = _lib.KERNELS[kernel]
-    args.flags = _lib.SAS_FWD_FLAG_CU_SEQLENS if layout_q == "TND" else 0
     if split_tiles < 0:
         raise ValueError("split_tiles must be >= 0")
-    args.split_tiles = int(split_tiles)
-
-    lib = _lib.load()
-    nbytes = _lib.ctypes.c_size_t(0)
-    _lib.check(lib.sas_workspace_size(_lib.ctypes.byref(args), _lib.ctypes.byref(nbytes)), "sas_workspace_size")
-    ws = _workspace(nbytes.value, dev)
-    out_user = None  # a caller's out that starts inside a 16-byte vector: written through a copy
-    if out is None:
-        out_flat = torch.empty((T, N1, Dv), dtype=q.dtype, device=dev)
+    ratio = int(cmp_ratio) if cmp_ratio is not None else 4
+    mq = -1 if max_seqlen_q is None else int(max_seqlen_q)
+    common = (q, ori_kv, cmp_kv, cmp_sparse_indices, ori_block_table, cmp_block_table, cu_seqlens_q, seqused_kv,
+              sinks, metadata, float(softmax_scale), ratio, int(ori_win_left), layout_q, Dv, kernel, mq,
+              int(split_tiles), bool(check_status))
+    if out is None and lse_out is None:
+        out_r, lse_r = torch.ops.sas_b200.sparse_attn_sharedkv(*common)
     else:
-        out_flat = out.view(T, N1, Dv)
-        if out_flat.data_ptr() % 16:
-            out_user, out_flat = out_flat, torch.empty_like(out_flat)
-    if lse_out is None:
-        lse_flat = torch.empty((T, N1), dtype=torch.float32, device=dev)
-    else:
-        lse_flat = lse_out.view(T, N1)
-    q_c = _dense16(q_flat)
-    stream = torch.cuda.current_stream(dev).cuda_stream
-    rc = lib.sas_forward(
-        _lib.ctypes.byref(args),
-        _ptr(q_c),
-        _ptr(ori_kv_d),
-        _ptr(ori_bt),
-        _ptr(cmp_kv_d),
-        _ptr(cmp_bt),
-        _ptr(idx_flat),
-        _ptr(q_prefix),
-        _ptr(act_q),
-        _ptr(seq_kv),
-        _ptr(sinks_d),
-        _ptr(metadata),
-        _ptr(out_flat),
-        _ptr(lse_flat),
-        _ptr(ws),
-        ws.numel(),
-        stream,
-    )
-    _lib.check(rc, "sas_forward")
-    if out_user is not None:
-        out_user.copy_(out_flat)
-        out_flat = out_user
-    if check_status:
-        st = _lib.ctypes.c_uint32(0)
-        _lib.check(lib.sas_read_status(_ptr(ws), _lib.ctypes.byref(st), stream), "sas_read_status")
-        if st.value:
-            raise RuntimeError(f"sas_forward device status: {_lib.status_names(st.value)}")
-
-    if layout_q == "TND":
-        out_r, lse_r = out_flat, lse_flat
-    else:
-        out_r = out_flat.reshape(B, T // max(B, 1), N1, Dv)
-        lse_r = lse_flat.reshape(B, T // max(B, 1), N1)
+        o_shape, l_shape = _out_shapes(q, layout_q, Dv)
+        out_r = out.view(o_shape) if out is not None else torch.empty(o_shape, dtype=q.dtype, device=q.device)
+        lse_r = lse_out.view(l_shape) if lse_out is not None else torch.empty(l_shape, dtype=torch.float32,
+                                                                             device=q.device)
+        torch.ops.sas_b200.sparse_attn_sharedkv_out(*common, out_r, lse_r)
     if return_softmax_lse:
         return out_r, lse_r
     return out_r

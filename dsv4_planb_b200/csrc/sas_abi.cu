@@ -17,14 +17,14 @@ namespace sas_host {
 int launch_prep(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const int32_t *cmp_bt, const int32_t *idx,
                 const int32_t *q_prefix, const int32_t *act_q, const int32_t *act_kv, cudaStream_t s);
 int launch_fwd_simt(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const void *q, const void *ori_kv,
-                    const int32_t *ori_bt, const void *cmp_kv, const float *sinks, void *out, float *lse,
-                    cudaStream_t s);
+                    const int32_t *ori_bt, const void *cmp_kv, const int32_t *cmp_bt, const float *sinks, void *out,
+                    float *lse, cudaStream_t s);
 bool tc_supported(const SasFwdArgs &a);
 size_t tc_workspace(const SasFwdArgs &a);
 int tc_kernel_count(const SasFwdArgs &a);
 int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const void *q, const void *ori_kv,
-                  const int32_t *ori_bt, const void *cmp_kv, const float *sinks, void *out, float *lse,
-                  cudaStream_t s);
+                  const int32_t *ori_bt, const void *cmp_kv, const int32_t *cmp_bt, const float *sinks, void *out,
+                  float *lse, cudaStream_t s);
 
 int check_cuda(cudaError_t e) {
     if (e == cudaSuccess) return SAS_OK;
@@ -61,9 +61,11 @@ int validate_fwd(const SasFwdArgs &a) {
     return SAS_OK;
 }
 
-sas::FwdLayout fwd_layout(const SasFwdArgs &a) {
+// cfa_rows: also room for scenario 2's compressed rows (max_cmp_len per token), which only the
+// sas_resolve_rows export writes; the attention kernels resolve CFA rows through the table directly.
+sas::FwdLayout fwd_layout(const SasFwdArgs &a, bool cfa_rows) {
     sas::FwdLayout L{};
-    L.row_cap = a.scenario == 3 ? a.topk : (a.scenario == 2 ? a.max_cmp_len : 0);
+    L.row_cap = a.scenario == 3 ? a.topk : (a.scenario == 2 && cfa_rows ? a.max_cmp_len : 0);
     const size_t T = (size_t)(a.num_tokens > 0 ? a.num_tokens : 0);
     size_t off = 0;
     auto take = [&](size_t bytes) { size_t o = off; off = sas::align_up(off + bytes); return o; };
@@ -117,7 +119,7 @@ int sas_workspace_size(const SasFwdArgs *args, size_t *bytes) {
     if (!args || !bytes) return SAS_ERR_INVALID_ARG;
     int rc = validate_fwd(*args);
     if (rc) return rc;
-    *bytes = fwd_layout(*args).total;
+    *bytes = fwd_layout(*args, true).total;  // enough for sas_forward and for sas_resolve_rows
     return SAS_OK;
 }
 
@@ -186,8 +188,8 @@ int sas_forward(const SasFwdArgs *args, const void *q, const void *ori_kv, const
     rc = launch_prep(a, L, ws, cmp_block_table, cmp_indices, q_prefix, act_q_len, act_kv_len, s);
     if (rc) return rc;
     if ((rc = record_kernel_event(true, s))) return rc;
-    if (use_tc(a)) rc = launch_fwd_tc(a, L, ws, q, ori_kv, ori_block_table, cmp_kv, sinks, out, lse, s);
-    else rc = launch_fwd_simt(a, L, ws, q, ori_kv, ori_block_table, cmp_kv, sinks, out, lse, s);
+    if (use_tc(a)) rc = launch_fwd_tc(a, L, ws, q, ori_kv, ori_block_table, cmp_kv, cmp_block_table, sinks, out, lse, s);
+    else rc = launch_fwd_simt(a, L, ws, q, ori_kv, ori_block_table, cmp_kv, cmp_block_table, sinks, out, lse, s);
     if (rc) return rc;
     return record_kernel_event(false, s);
 }
@@ -210,7 +212,7 @@ int sas_resolve_rows(const SasFwdArgs *args, const int32_t *ori_block_table, con
     rc = check_inputs(a, ori_block_table, ori_block_table, cmp_block_table, cmp_block_table, cmp_indices, q_prefix,
                       act_q_len, act_kv_len);
     if (rc) return rc;
-    const sas::FwdLayout L = fwd_layout(a);
+    const sas::FwdLayout L = fwd_layout(a, true);
     if (!workspace || workspace_bytes < L.total) return SAS_ERR_WORKSPACE;
     if (a.num_tokens > 0 && !token_info) return SAS_ERR_INVALID_ARG;
     rc = check_alignment(nullptr, nullptr, ori_block_table, nullptr, cmp_block_table, cmp_indices, q_prefix,

@@ -6,6 +6,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
+
 #include "sas_b200.h"
 
 namespace sas {
@@ -46,6 +49,23 @@ constexpr uint32_t kSpinLimit = 1u << 26;
 
 // Devices a process may drive (per-device launch attribute caches).
 constexpr int kMaxDevices = 64;
+
+// First-time set-up per device (kernel attributes belong to a device's context).  Each bit of
+// `done` marks one finished step; `run` performs a step under a mutex the first time, so host
+// threads that make their first calls at once neither race on the flags nor launch before the
+// attribute is raised.  Steps are idempotent: after a context reset a repeat would be harmless.
+struct DeviceOnce {
+    std::atomic<uint32_t> done{0};
+    std::mutex mu;
+    template <typename F> int run(uint32_t bit, F &&step) {
+        if (done.load(std::memory_order_acquire) & bit) return 0;
+        std::lock_guard<std::mutex> lock(mu);
+        if (done.load(std::memory_order_relaxed) & bit) return 0;
+        const int rc = step();
+        if (rc == 0) done.fetch_or(bit, std::memory_order_release);
+        return rc;
+    }
+};
 
 template <typename T> struct DT;
 template <> struct DT<__nv_bfloat16> {
@@ -99,6 +119,6 @@ __device__ __forceinline__ int64_t paged_row(const int32_t *__restrict__ table, 
 // Host-side helpers shared by the launch code.
 namespace sas_host {
 int check_cuda(cudaError_t e);
-sas::FwdLayout fwd_layout(const SasFwdArgs &a);
+sas::FwdLayout fwd_layout(const SasFwdArgs &a, bool cfa_rows = false);
 int validate_fwd(const SasFwdArgs &a);
 } // namespace sas_host

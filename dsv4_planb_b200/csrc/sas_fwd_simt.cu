@@ -23,12 +23,14 @@ constexpr int kMaxPairs = 16; // D_v / 32 <= 16
 struct SimtArgs {
     const void *q, *ori, *cmp;
     const int32_t *ori_bt, *tinfo, *rows;
+    const int32_t *cmp_bt;  // scenario 2: compressed rows are positions 0 .. n_cmp-1 of this table
     const float *sinks;
     void *out;
     float *lse;
     uint32_t *status;
     int T, N1, Dq, Dv, row_cap;
     int ori_block_num, ori_block_size, ori_table_len;
+    int dense_cmp, cmp_block_num, cmp_block_size, cmp_table_len;
     float scale_log2;
 };
 
@@ -97,7 +99,9 @@ __global__ void __launch_bounds__(kThreads) fwd_simt_kernel(SimtArgs p) {
                                    p.status);
                 src = 0;
             } else if (slot < n_keys) {
-                r = crow[slot - n_win];
+                r = p.dense_cmp ? sas::paged_row(p.cmp_bt, b, p.cmp_table_len, p.cmp_block_size, p.cmp_block_num,
+                                                 slot - n_win, p.status)
+                                : crow[slot - n_win];
                 src = 1;
             }
             rid[tid] = r;
@@ -214,8 +218,8 @@ size_t simt_smem(int Dq) {
 namespace sas_host {
 
 int launch_fwd_simt(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const void *q, const void *ori_kv,
-                    const int32_t *ori_bt, const void *cmp_kv, const float *sinks, void *out, float *lse,
-                    cudaStream_t s) {
+                    const int32_t *ori_bt, const void *cmp_kv, const int32_t *cmp_bt, const float *sinks, void *out,
+                    float *lse, cudaStream_t s) {
     if (a.num_tokens == 0 || a.num_heads == 0) return SAS_OK;
     SimtArgs p;
     p.q = q;
@@ -236,6 +240,11 @@ int launch_fwd_simt(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, cons
     p.ori_block_num = a.ori_block_num;
     p.ori_block_size = a.ori_block_size;
     p.ori_table_len = a.ori_table_len;
+    p.dense_cmp = a.scenario == 2 ? 1 : 0;
+    p.cmp_bt = cmp_bt;
+    p.cmp_block_num = a.cmp_block_num;
+    p.cmp_block_size = a.cmp_block_size;
+    p.cmp_table_len = a.cmp_table_len;
     p.scale_log2 = a.softmax_scale * 1.4426950408889634f;
     const size_t smem = simt_smem(a.head_dim);
     dim3 grid(a.num_tokens, (a.num_heads + kHG - 1) / kHG);
@@ -244,17 +253,17 @@ int launch_fwd_simt(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, cons
     int dev = 0;
     if (check_cuda(cudaGetDevice(&dev))) return SAS_ERR_CUDA;
     if (dev < 0 || dev >= sas::kMaxDevices) return SAS_ERR_UNSUPPORTED;
-    static bool attr_done[sas::kMaxDevices][2] = {};
+    static sas::DeviceOnce attr_done[sas::kMaxDevices];
     const int di = a.dtype == SAS_DTYPE_BF16 ? 0 : 1;
-    if (!attr_done[dev][di]) {
+    const int rc = attr_done[dev].run(1u << di, [&] {
         const int max_smem = (int)simt_smem(1024);
         cudaError_t e = di == 0 ? cudaFuncSetAttribute(fwd_simt_kernel<__nv_bfloat16>,
                                                        cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem)
                                 : cudaFuncSetAttribute(fwd_simt_kernel<__half>,
                                                        cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-        if (check_cuda(e)) return SAS_ERR_CUDA;
-        attr_done[dev][di] = true;
-    }
+        return check_cuda(e);
+    });
+    if (rc) return rc;
     if (a.dtype == SAS_DTYPE_BF16) fwd_simt_kernel<__nv_bfloat16><<<grid, kThreads, smem, s>>>(p);
     else fwd_simt_kernel<__half><<<grid, kThreads, smem, s>>>(p);
     return check_cuda(cudaGetLastError());

@@ -25,10 +25,11 @@
 // Keys of a token are its window rows (padded to a multiple of 64) followed by
 // its resolved compressed rows (sas_prep.cu); masked / unmapped rows are read
 // as zeros (the gather points them past the pool).  Scores live in the
-// log2 domain.  The running max is only raised when a tile's max exceeds it by
-// more than 8 (P <= 2^8, exact in bf16 and fp32), so O is rarely rescaled; the
-// final out = O / l and lse = (m + log2 l) ln 2 equal the reference golden
-// (golden.py:156-200) up to rounding.
+// log2 domain.  The running max follows every increase (P <= 1), so P is
+// rounded to bf16 at the scale of the exact running max, as the reference
+// golden rounds it (golden.py:186-194); the output CTA rescales the rows of O
+// whose max rose.  The final out = O / lr and lse = (m + log2 l) ln 2 equal
+// the golden up to rounding.
 //
 // Every wait is bounded by %globaltimer; a timeout sets SAS_STATUS_WAIT_TIMEOUT,
 // raises an abort flag in both CTAs and lets every role fall through to the
@@ -37,6 +38,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <atomic>
 #include <type_traits>
 
 #include "sas_common.cuh"
@@ -54,7 +56,13 @@ constexpr int kThreads = 288;       // warps 0-3 softmax / epilogue, 4-7 gather,
 constexpr int kChunkBytes = kBK * 128;  // one 64-column slab of a 64-row tile (128B-swizzled)
 constexpr int kMaxDq = 576;
 constexpr int kMaxDv = 512;
-constexpr float kTau = 8.0f;      // lazy-rescale threshold (log2 units)
+// Rescale threshold of the running max (log2 units): 0 = raise it on every increase.  A lazy
+// threshold (FlashAttention-4 style; 8 keeps P <= 256) rescales O less often, but rounds P to bf16
+// at another scale than the reference golden, whose P have a row maximum of exactly 1: with 8, the
+// reference paramsets' low-precision acceptance (>= 99.5 % of elements within bf16 rtol 2^-7 of the
+// golden's bf16 output) fell to 99.18-99.67 %; with 0 it is 99.84-99.96 % (CPU emulation of this
+// kernel's arithmetic on the reference paramsets).
+constexpr float kTau = 0.0f;
 constexpr uint64_t kTimeoutNs = 4000000000ull;
 
 // P message: bf16 P [128 heads][64 keys] (SW128 K-major) + per-head floats.
@@ -136,12 +144,15 @@ struct TcArgs {
     const void *q;
     const uint8_t *ori, *cmp;  // paged pools, rows of D_qk elements
     const int32_t *ori_bt, *tinfo, *rows;
+    const int32_t *cmp_bt;   // scenario 2: compressed rows are positions 0 .. n_cmp-1 of this table
     const float *sinks;
     void *out;
     float *lse;
     uint32_t *status;
     int T, N1, Dq, Dv, row_cap;
     int ori_block_num, ori_block_size, ori_table_len;
+    int dense_cmp;           // scenario 2 (CFA): resolve compressed rows through cmp_bt here
+    int cmp_block_num, cmp_block_size, cmp_table_len;
     int ori_rows, cmp_rows;  // rows of each pool: the out-of-range row index reads zeros
     int test_stall;          // SAS_FWD_FLAG_TEST_STALL: withhold the first P-slot release
     int *counter;            // next unit to hand out (zeroed with the status word before the launch)
@@ -233,14 +244,16 @@ __device__ __forceinline__ bool wait_warp(const Sync &s, uint32_t bar, uint32_t 
 }
 
 // Warp-uniform poll: true (for every lane, each having acquired the phase) once
-// any lane sees the phase complete.  A completed phase stays complete until
-// this warp arrives elsewhere, so the lanes that lagged succeed at once.
+// any lane sees the phase complete.  Used on rs_req and o_full, whose next phase
+// needs an arrival this warp makes later (rs_done / o_empty), so a phase one
+// lane saw complete stays complete and the lanes that lagged acquire it on their
+// first test.  The bound only guards that argument; it never binds.
 __device__ __forceinline__ bool poll_warp(uint32_t bar, uint32_t parity) {
     // test_wait never suspends: a try_wait on one barrier could sleep through the other's phase
     const bool mine = mbar_test(bar, parity);
     if (!__any_sync(0xffffffffu, mine)) return false;
     if (!mine)
-        while (!mbar_try(bar, parity)) {
+        for (uint32_t i = 0; i < (1u << 16) && !mbar_test(bar, parity); ++i) {
         }
     return true;
 }
@@ -300,35 +313,52 @@ __device__ __forceinline__ bool tq_publish(const TcArgs &p, const Sync &sy, uint
 }
 
 // Row lookup of key k of tile j of an item, split in two so that the global
-// load (a block-table entry for window keys, a resolved row for compressed
-// keys) is issued one tile ahead and its latency hides behind the copies of
-// the current tile.  key_fetch issues the load; key_row turns its value into
-// the physical row, or -1 (masked / unmapped: read as zeros).
+// load (a block-table entry for window keys and for the dense compressed range
+// of CFA, a resolved row for SCFA's compressed keys) is issued one tile ahead
+// and its latency hides behind the copies of the current tile.  key_fetch
+// issues the load; key_row turns its value into the physical row, or -1
+// (masked / unmapped: read as zeros).
+__device__ __forceinline__ int32_t table_fetch(const int32_t *table, int b, int table_len, int block_size,
+                                               int64_t pos) {
+    const int64_t blk = pos / block_size;
+    if (pos < 0 || blk >= table_len) return -1;
+    return __ldg(table + (int64_t)b * table_len + blk);
+}
+
+// Physical row of logical position `pos` of a paged pool, from the table entry table_fetch loaded.
+__device__ __forceinline__ int32_t table_row(const TcArgs &p, int64_t pos, int block_size, int table_len,
+                                             int block_num, int32_t fetched) {
+    if (pos < 0) return -1;
+    const int64_t blk = pos / block_size;
+    if (blk >= table_len || (fetched < 0 && fetched != -1) || fetched >= block_num) {
+        sas::set_status(p.status, SAS_STATUS_BAD_BLOCK);
+        return -1;
+    }
+    if (fetched < 0) return -1;
+    return (int32_t)((int64_t)fetched * block_size + (pos - blk * block_size));
+}
+
 __device__ __forceinline__ int32_t key_fetch(const TcArgs &p, const Item &it, const int32_t *crow, int j, int k) {
     if (j < it.nwt) {
         const int slot = j * kBK + k;
         if (slot >= it.n_win) return -1;
-        const int64_t blk = ((int64_t)it.left + slot) / p.ori_block_size;
-        if (it.left + slot < 0 || blk >= p.ori_table_len) return -1;
-        return __ldg(p.ori_bt + (int64_t)it.b * p.ori_table_len + blk);
+        return table_fetch(p.ori_bt, it.b, p.ori_table_len, p.ori_block_size, (int64_t)it.left + slot);
     }
     const int c = (j - it.nwt) * kBK + k;
-    return c < it.n_cmp ? __ldg(crow + c) : -1;
+    if (c >= it.n_cmp) return -1;
+    return p.dense_cmp ? table_fetch(p.cmp_bt, it.b, p.cmp_table_len, p.cmp_block_size, c) : __ldg(crow + c);
 }
 
 __device__ __forceinline__ int32_t key_row(const TcArgs &p, const Item &it, int j, int k, int32_t fetched) {
     if (j < it.nwt) {
         const int slot = j * kBK + k;
         if (slot >= it.n_win) return -1;
-        const int64_t pos = (int64_t)it.left + slot;
-        if (pos < 0) return -1;
-        const int64_t blk = pos / p.ori_block_size;
-        if (blk >= p.ori_table_len || (fetched < 0 && fetched != -1) || fetched >= p.ori_block_num) {
-            sas::set_status(p.status, SAS_STATUS_BAD_BLOCK);
-            return -1;
-        }
-        if (fetched < 0) return -1;
-        return (int32_t)((int64_t)fetched * p.ori_block_size + (pos - blk * p.ori_block_size));
+        return table_row(p, (int64_t)it.left + slot, p.ori_block_size, p.ori_table_len, p.ori_block_num, fetched);
+    }
+    if (p.dense_cmp) {
+        const int c = (j - it.nwt) * kBK + k;
+        if (c >= it.n_cmp) return -1;
+        return table_row(p, c, p.cmp_block_size, p.cmp_table_len, p.cmp_block_num, fetched);
     }
     return fetched >= 0 ? fetched : -1;
 }
@@ -689,7 +719,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
                     float alpha = 1.f;
-                    bool need = false;
                     if (j == it.j0) {  // every tile has a valid key, so mn is finite
                         const float mn = fmaxf(m, mx);
                         const float a0 = exp2f(m - mn);
@@ -701,7 +730,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                         l *= alpha;
                         lr *= alpha;
                         m = mx;
-                        need = true;
                     }
                     uint32_t pk[32];
                     float sum4[4] = {0.f, 0.f, 0.f, 0.f}, sumr4[4] = {0.f, 0.f, 0.f, 0.f};
@@ -725,8 +753,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     l += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
                     lr += (sumr4[0] + sumr4[1]) + (sumr4[2] + sumr4[3]);
-                    (void)need;
-                    const bool last = j == it.j1 - 1;
                     const int ps = pc % kPStages;
                     if (!wait_warp(sy, smem_u32(&hd->p_empty[ps]), ((pc / kPStages) & 1) ^ 1, true)) goto done;
                     const uint32_t msg = msg0 + ps * kMsgBytes;
@@ -744,7 +770,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                         st_async_u32(msg + kMsgStats + 4 * stat_index<false>(h, kMsgL), __float_as_uint(lr), pbar);
                         st_async_u32(msg + kMsgStats + 4 * stat_index<false>(h, kMsgM), __float_as_uint(m), pbar);
                     }
-                    (void)last;
                 }
                 if (it.np == 1 && p.lse && h < p.N1)
                     p.lse[(int64_t)t * p.N1 + h] = (m + log2f(l)) * 0.6931471805599453f;
@@ -781,13 +806,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int ps = pc % kPStages, vs = vc % kVStages;
                     if (!wait_warp(sy, smem_u32(&hd->p_full[ps]), (pc / kPStages) & 1, true)) goto done;
                     if (lane == 0) mbar_arrive_expect_tx(smem_u32(&hd->p_full[ps]), msg_tx<kSplit>());  // next message
-                    if (!wait_warp(sy, smem_u32(&hd->v_full[vs]), (vc / kVStages) & 1)) goto done;
                     uint8_t *msg = msgs + ps * kMsgBytes;
                     bool need = false;
                     for (int i = lane; i < 128; i += 32)
                         need |= reinterpret_cast<const float *>(msg + kMsgStats)[stat_index<kSplit>(i, kMsgAlpha)] != 1.f;
-                    if (__any_sync(0xffffffffu, need) && j > it.j0) {
-                        // rescale O: wait for every PV product so far, then let warps 4-7 scale the rows
+                    const bool rescale = __any_sync(0xffffffffu, need) && j > it.j0;
+                    if (rescale) {
+                        // rescale O: wait for every PV product so far, then let warps 0-3 scale the rows
+                        // (their TMEM round trip overlaps the wait for this tile's V)
                         if (lane == 0) tc_commit(smem_u32(&hd->pv_done));
                         __syncwarp();
                         if (!wait_warp(sy, smem_u32(&hd->pv_done), pvc & 1)) goto done;
@@ -797,6 +823,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                             mbar_arrive(smem_u32(&hd->rs_req));
                         }
                         __syncwarp();
+                    }
+                    if (!wait_warp(sy, smem_u32(&hd->v_full[vs]), (vc / kVStages) & 1)) goto done;
+                    if (rescale) {
                         if (!wait_warp(sy, smem_u32(&hd->rs_done), rsc & 1)) goto done;
                         ++rsc;
                     }
@@ -864,13 +893,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const float a =
                             reinterpret_cast<const float *>(msgs + hd->rs_stage * kMsgBytes + kMsgStats)[stat_index<kSplit>(h, kMsgAlpha)];
                         if (__any_sync(0xffffffffu, a != 1.f)) {
-                            for (int c = 0; c < p.Dv / 32; ++c) {
-                                uint32_t r[32];
-                                tmem_ld32(tmem + lane_base + c * 32, r);
+                            // four 32-column loads in flight per wait: the loop is bound by TMEM
+                            // latency, not bandwidth (one wait per 32 columns doubled the cost)
+                            for (int c = 0; c < p.Dv / 32; c += 4) {
+                                uint32_t r0[32], r1[32], r2[32], r3[32];
+                                tmem_ld32(tmem + lane_base + c * 32, r0);
+                                tmem_ld32(tmem + lane_base + (c + 1) * 32, r1);
+                                tmem_ld32(tmem + lane_base + (c + 2) * 32, r2);
+                                tmem_ld32(tmem + lane_base + (c + 3) * 32, r3);
                                 tc_wait_ld();
 #pragma unroll
-                                for (int k = 0; k < 32; ++k) r[k] = __float_as_uint(__uint_as_float(r[k]) * a);
-                                tmem_st32(tmem + lane_base + c * 32, r);
+                                for (int k = 0; k < 32; ++k) {
+                                    r0[k] = __float_as_uint(__uint_as_float(r0[k]) * a);
+                                    r1[k] = __float_as_uint(__uint_as_float(r1[k]) * a);
+                                    r2[k] = __float_as_uint(__uint_as_float(r2[k]) * a);
+                                    r3[k] = __float_as_uint(__uint_as_float(r3[k]) * a);
+                                }
+                                tmem_st32(tmem + lane_base + c * 32, r0);
+                                tmem_st32(tmem + lane_base + (c + 1) * 32, r1);
+                                tmem_st32(tmem + lane_base + (c + 2) * 32, r2);
+                                tmem_st32(tmem + lane_base + (c + 3) * 32, r3);
                             }
                             tc_wait_st();
                         }
@@ -1106,8 +1148,8 @@ size_t tc_workspace(const SasFwdArgs &a) {
 }
 
 int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const void *q, const void *ori_kv,
-                  const int32_t *ori_bt, const void *cmp_kv, const float *sinks, void *out, float *lse,
-                  cudaStream_t s) {
+                  const int32_t *ori_bt, const void *cmp_kv, const int32_t *cmp_bt, const float *sinks, void *out,
+                  float *lse, cudaStream_t s) {
     if (a.num_tokens == 0) return SAS_OK;
     const bool bf16 = a.dtype == SAS_DTYPE_BF16;
     TcArgs p;
@@ -1129,6 +1171,11 @@ int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const 
     p.ori_block_num = a.ori_block_num;
     p.ori_block_size = a.ori_block_size;
     p.ori_table_len = a.ori_table_len;
+    p.dense_cmp = a.scenario == 2 ? 1 : 0;
+    p.cmp_bt = cmp_bt;
+    p.cmp_block_num = a.cmp_block_num;
+    p.cmp_block_size = a.cmp_block_size;
+    p.cmp_table_len = a.cmp_table_len;
     p.ori_rows = a.ori_block_num * a.ori_block_size;
     p.cmp_rows = a.scenario >= 2 ? a.cmp_block_num * a.cmp_block_size : p.ori_rows;
     p.scale_log2 = a.softmax_scale * 1.4426950408889634f;
@@ -1157,18 +1204,19 @@ int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const 
     int dev = 0;
     if (check_cuda(cudaGetDevice(&dev))) return SAS_ERR_CUDA;
     if (dev < 0 || dev >= sas::kMaxDevices) return SAS_ERR_UNSUPPORTED;
-    static uint8_t attr_done[sas::kMaxDevices] = {};
-    static int num_sms[sas::kMaxDevices] = {};
+    static sas::DeviceOnce attr_done[sas::kMaxDevices];
+    static std::atomic<int> num_sms[sas::kMaxDevices] = {};
     const int di = (bf16 ? 0 : 2) + (p.P > 1 ? 1 : 0);
-    if (!(attr_done[dev] & (1u << di))) {
-        if (check_cuda(cudaFuncSetAttribute(kernels[di], cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes)))
-            return SAS_ERR_CUDA;
-        attr_done[dev] |= (uint8_t)(1u << di);
+    int rc_attr = attr_done[dev].run(1u << di, [&] {
+        return check_cuda(cudaFuncSetAttribute(kernels[di], cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+    });
+    if (rc_attr) return rc_attr;
+    int sms = num_sms[dev].load(std::memory_order_relaxed);
+    if (!sms) {
+        if (check_cuda(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev))) return SAS_ERR_CUDA;
+        num_sms[dev].store(sms, std::memory_order_relaxed);
     }
-    if (!num_sms[dev] &&
-        check_cuda(cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev)))
-        return SAS_ERR_CUDA;
-    const int clusters = std::max(1, std::min(p.U, num_sms[dev] / 2));
+    const int clusters = std::max(1, std::min(p.U, sms / 2));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * clusters, 1, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);

@@ -9,7 +9,9 @@
 //               the first -1 stops the scan, an index >= thr is skipped, duplicates
 //               stay (golden.py:41-62).  An index < -1 is outside the contract: it
 //               is skipped and SAS_STATUS_BAD_INDEX is raised.
-//   CFA (2)     positions 0 .. thr-1 (golden.py:146-150)
+//   CFA (2)     positions 0 .. thr-1 (golden.py:146-150): only the count is recorded;
+//               the attention kernels map the positions through the table themselves
+//               (the rows are written only for the sas_resolve_rows export)
 //   SWA (1)     no compressed keys
 // Each kept position p maps through the cmp block table to a physical row
 // (table[b][p / bs] * bs + p % bs); an unmapped block gives -1, which the
@@ -112,7 +114,7 @@ __global__ void __launch_bounds__(kThreads, 1) prep_kernel(PrepArgs p) {
     const int q0 = __ldg(p.q_prefix + b);
     const int aq = p.cu ? __ldg(p.q_prefix + b + 1) - q0 : __ldg(p.act_q + b);
     const int akv = __ldg(p.act_kv + b);
-    const bool staged = p.scenario >= 2 && p.cmp_table_len <= kTableSmem;
+    const bool staged = (p.scenario == 3 || (p.scenario == 2 && p.row_cap > 0)) && p.cmp_table_len <= kTableSmem;
     int32_t tabv[kTableSmem / kThreads];
 #pragma unroll
     for (int k = 0; k < kTableSmem / kThreads; ++k) {
@@ -153,9 +155,11 @@ __global__ void __launch_bounds__(kThreads, 1) prep_kernel(PrepArgs p) {
         const int32_t *tab = staged ? tab_s : nullptr;
         const int thr = floordiv_i(akv - aq + s + 1, p.ratio);
         if (p.scenario == 2) {
-            if (thr > p.row_cap && tid == 0) sas::set_status(p.status, SAS_STATUS_BAD_TOKEN);
-            n_cmp = min(max(thr, 0), p.row_cap);
-            for (int i = tid; i < n_cmp; i += kThreads) rows[i] = cmp_row(p, tab, b, i);
+            n_cmp = max(thr, 0);
+            if (p.row_cap > 0) {  // the export: as many rows as the caller's max_cmp_len holds
+                if (thr > p.row_cap && tid == 0) sas::set_status(p.status, SAS_STATUS_BAD_TOKEN);
+                for (int i = tid; i < min(n_cmp, p.row_cap); i += kThreads) rows[i] = cmp_row(p, tab, b, i);
+            }
         } else {
             const int n_scan = min(p.K, thr);
             const int32_t *ir = p.idx + t * (int64_t)p.K;

@@ -64,7 +64,10 @@ typedef struct SasFwdArgs {
     int32_t topk;           /* K: last dim of cmp_indices (scenario 3) */
     int32_t cmp_ratio;      /* compression ratio (scenarios 2, 3) */
     int32_t scenario;       /* 1 SWA, 2 CFA, 3 SCFA (api.py:196-202) */
-    int32_t max_cmp_len;    /* scenario 2: >= max over requests of floor(act_kv / cmp_ratio) */
+    int32_t max_cmp_len;    /* scenario 2, sas_resolve_rows only: row capacity of its cmp_rows
+                               export (>= max over requests of floor(act_kv / cmp_ratio)).
+                               sas_forward needs no bound (0 is fine): it resolves CFA's dense
+                               compressed range through the table in the attention kernel */
     int32_t ori_win_left;   /* sliding window: keys [s_g - ori_win_left, s_g] */
     int32_t ori_win_right;  /* must be 0 */
     int32_t ori_mask_mode;  /* must be 4 (band) */
@@ -186,11 +189,13 @@ int sas_read_status(const void *workspace, uint32_t *status, void *stream);
  *   - Calls whose sas_workspace_size exceeds SAS_NOALLOC_SCRATCH_BYTES are
  *     rejected with SAS_ERR_WORKSPACE (use sas_forward for those).
  *   - The first call on a device looks up the array's device address on the
- *     current device; make that first call before any stream capture.
+ *     current device; make that first call before any stream capture.  The
+ *     address is cached per device and CUDA context: after a cudaDeviceReset
+ *     the next call looks it up again (again outside any capture).
  *   - Every call shares the one array: calls that overlap on the GPU (other
  *     streams, other host threads) race.  Serialise them on one stream.
- *   - sas_read_status cannot be used with it (the status word lives in the
- *     private scratch).
+ *   - The device status word lives in the private scratch: read it with
+ *     sas_noalloc_read_status, not sas_read_status.
  * No counterpart in the reference.
  */
 #define SAS_NOALLOC_SCRATCH_BYTES (16u << 20)
@@ -198,6 +203,14 @@ int sas_forward_noalloc(const SasFwdArgs *args, const void *q, const void *ori_k
                         const void *cmp_kv, const int32_t *cmp_block_table, const int32_t *cmp_indices,
                         const int32_t *q_prefix, const int32_t *act_q_len, const int32_t *act_kv_len,
                         const float *sinks, const int32_t *metadata, void *out, float *lse, void *stream);
+
+/*
+ * The device status word (SAS_STATUS_* bits) the last sas_forward_noalloc call
+ * on the current device left in the library's scratch array: bad indices or
+ * table entries, or a bounded wait that gave up.  Synchronises `stream`;
+ * allocates nothing.  No counterpart in the reference.
+ */
+int sas_noalloc_read_status(uint32_t *status, void *stream);
 
 /* ---- metadata scheduler ----------------------------------------------------
  * Replaces sparse_attn_sharedkv_metadata (metadata.py:1018-1086, the Python

@@ -221,7 +221,7 @@ def test_strerror_and_version(lib):
 
 
 def test_api_rehomes_views_that_start_inside_a_vector():
-    # The Python layer hands the C ABI only 16-byte aligned q / pool bases: a view at an odd element
+    # The Python layer hands the C ABI only 16-byte aligned q bases: a view at an odd element
     # offset is copied (same values), an aligned one passes through untouched.
     import torch
 
@@ -236,3 +236,46 @@ def test_api_rehomes_views_that_start_inside_a_vector():
     assert torch.equal(fixed, odd)
     strided = base.view(8, 8)[:, :4]  # non-contiguous: made dense
     assert _dense16(strided).is_contiguous() and torch.equal(_dense16(strided), strided)
+
+
+def test_api_rejects_misaligned_or_strided_pools():
+    # A paged KV pool is never copied per call (it can be gigabytes): a pool view that starts
+    # inside a 16-byte vector, or is not contiguous, is an argument error.
+    import pytest
+    import torch
+
+    from dsv4_planb_b200.api import _pool16
+
+    base = torch.zeros(4 * 128 * 576 + 1, dtype=torch.bfloat16)
+    good = base[:-1].view(4, 128, 1, 576)
+    assert _pool16(good, "ori_kv") is good
+    with pytest.raises(ValueError, match="16-byte"):
+        _pool16(base[1:].view(4, 128, 1, 576), "ori_kv")
+    with pytest.raises(ValueError, match="contiguous"):
+        _pool16(good.transpose(0, 1), "cmp_kv")
+
+
+def test_registered_op_fake_shapes():
+    # The op is registered with the dispatcher; its fake (meta) implementation gives the output
+    # shapes and dtypes without a device, which is what torch.compile traces against.
+    import torch
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    import dsv4_planb_b200.api  # noqa: F401  (registers the ops)
+
+    with FakeTensorMode():
+        q = torch.empty(6, 128, 576, dtype=torch.bfloat16)
+        pool = torch.empty(10, 128, 1, 576, dtype=torch.bfloat16)
+        bt = torch.empty(2, 5, dtype=torch.int32)
+        idx = torch.empty(6, 1, 2048, dtype=torch.int32)
+        cu = torch.empty(3, dtype=torch.int32)
+        kv = torch.empty(2, dtype=torch.int32)
+        sinks = torch.empty(128, dtype=torch.float32)
+        out, lse = torch.ops.sas_b200.sparse_attn_sharedkv(q, pool, pool, idx, bt, bt, cu, kv, sinks, None, 0.04, 4,
+                                                           127, "TND", 512, "auto", 3, 0, False)
+        assert out.shape == (6, 128, 512) and out.dtype == torch.bfloat16
+        assert lse.shape == (6, 128) and lse.dtype == torch.float32
+        qb = torch.empty(2, 3, 128, 576, dtype=torch.bfloat16)
+        out, lse = torch.ops.sas_b200.sparse_attn_sharedkv(qb, pool, None, None, bt, None, None, kv, sinks, None,
+                                                           0.04, 4, 127, "BSND", 512, "tc", -1, 0, False)
+        assert out.shape == (2, 3, 128, 512) and lse.shape == (2, 3, 128)

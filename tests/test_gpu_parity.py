@@ -107,22 +107,22 @@ def test_reference_paramsets(api, cuda_device, kernel, fixture_name):
     lse = lse.cpu().numpy()
     toks = case["tokens"]
     # The reference test's own acceptance, against its low-precision golden
-    # (test_sparse_attn_sharedkv.py:394-467: >= 99.5% of elements within
-    # bf16 rtol 2^-7).  The tensor-core path raises its running max lazily, so
-    # its P are rounded at another scale than the golden's (whose row maximum is
-    # exactly 1.0): its distance to that rounded golden is rounding noise, not
-    # error against the fp32 result (checked strictly below).  Measured on
-    # B200: SIMT 99.63-99.85%, TC 99.18-99.67% over the reference paramsets.
+    # (test_sparse_attn_sharedkv.py:394-467): >= 99.5% of elements within bf16
+    # rtol 2^-7 and a worst normalised error below 10, for both kernels.  Both
+    # round P to bf16 at the scale of the exact running max, as the golden does.
     ref_low = F.low_bits_to_f32(case["out_low_bits"], tag)
     pct, max_rel = F.check_result(out[toks], ref_low, tag)
-    assert pct >= (99.5 if kernel == "simt" else 99.0) and max_rel < 10.0, (pct, max_rel)
-    pct, max_rel = F.check_lse(lse[toks], case["lse_low"], tag)
-    assert pct >= 99.5 and max_rel < 10.0, (pct, max_rel)
-    # north-star tolerance vs the fp32 golden (|scores| reach ~1e2 here: lse bar scaled by |lse|)
+    lpct, lmax_rel = F.check_lse(lse[toks], case["lse_low"], tag)
+    # north-star tolerance vs the fp32 golden: out atol 2e-2 / rtol 1e-2, lse absolute 1e-3
     exp_out, exp_lse = case["out_fp32"], case["lse_fp32"]
     err = np.abs(out[toks] - exp_out) - (OUT_ATOL + OUT_RTOL * np.abs(exp_out))
+    dlse = float(np.abs(lse[toks] - exp_lse).max())
+    print(f"\n[parity] {fixture_name} {kernel}: _check_result {pct:.3f}% (max_rel {max_rel:.3f}), "
+          f"_check_lse {lpct:.3f}%, max|dlse| vs fp32 golden {dlse:.2e}, max out excess {err.max():.2e}")
+    assert pct >= 99.5 and max_rel < 10.0, (pct, max_rel)
+    assert lpct >= 99.5 and lmax_rel < 10.0, (lpct, lmax_rel)
     assert err.max() <= 0, err.max()
-    assert (np.abs(lse[toks] - exp_lse) <= LSE_ATOL * np.maximum(1.0, np.abs(exp_lse))).all()
+    assert dlse <= LSE_ATOL, dlse
 
 
 @pytest.mark.parametrize("kernel", KERNELS)
@@ -215,30 +215,49 @@ def test_unmapped_blocks_read_as_zero_rows(api, cuda_device, kernel):
     assert_close_to_golden(out, lse, ref_out, ref_lse, "holes")
 
 
-@pytest.mark.parametrize("kernel", KERNELS)
-def test_full_size_decode_sampled(api, cuda_device, kernel):
-    """C2 at full size (B=64, N1=128, K=2048): sampled tokens against the oracle,
-    plus size-independent properties (finite, LSE >= sink, rows are convex
-    combinations so |out| <= max |V|)."""
+FULL_CONFIGS = [("c2", "tc"), ("c2", "simt"), ("c3", "tc"), ("c4", "tc"), ("c5", "tc")]
+
+
+@pytest.mark.parametrize("cfg,kernel", FULL_CONFIGS, ids=[f"{c}-{k}" for c, k in FULL_CONFIGS])
+def test_full_config_parity(api, cuda_device, cfg, kernel):
+    """Every BASELINE configuration at its stated size through the public API: c2 (64 decode
+    tokens, seq U[8K, 32K]), c3 (32 requests x q_len 2, seq U[4K, 64K]), c4 (4 x 8192 prefill tokens
+    on ctx U[0, 16K]) and c5 (512 requests, seq log-U[1K, 128K], ~20 GB of pools).  Stratified tokens
+    (every request of c2 / c3; c4's first tokens, window edge, the token where thr reaches top-k,
+    middle and end of every request; 64 c5 requests spread over the length order) against the fp32
+    oracle at the north-star bars, and size-independent properties on every token: finite, LSE at
+    least the sink (the sink is one of the softmax's terms), |out| within max |V| (rows are convex
+    combinations of V rows)."""
     if kernel == "tc" and not tc_available():
         pytest.skip("tensor-core path not built")
     from dsv4_planb_b200 import workloads as W
+    from tests import _sampled as SM
 
-    wl = W.config_workload("c2", device=cuda_device)
-    out, lse = run(api, wl, kernel, cuda_device)
-    assert np.isfinite(out).all() and np.isfinite(lse).all()
-    sinks = wl.sinks.cpu().numpy()
-    assert (lse >= sinks[None, :] - 1e-5).all()
-    assert np.abs(out).max() <= float(wl.ori_kv.abs().max().float().cpu()) + 1e-2
-    sample = [0, 17, 40, 63]
-    wl_c = wl.to("cpu")
-    ref_out, ref_lse, _ = O.sparse_attn_sharedkv_oracle(
-        wl_c.q, ori_kv=wl_c.ori_kv, ori_block_table=wl_c.ori_block_table, seqused_kv=wl_c.seqused_kv,
-        q_prefix=wl_c.cu_seqlens_q[:-1], act_q=wl_c.cu_seqlens_q[1:] - wl_c.cu_seqlens_q[:-1], sinks=wl_c.sinks,
-        softmax_scale=wl_c.softmax_scale, cmp_kv=wl_c.cmp_kv, cmp_block_table=wl_c.cmp_block_table,
-        cmp_sparse_indices=wl_c.cmp_sparse_indices, cmp_ratio=wl_c.cmp_ratio, v_head_dim=wl_c.v_head_dim,
-        tokens=sample)
-    assert_close_to_golden(out[sample], lse[sample], ref_out[sample], ref_lse[sample], "c2 sampled")
+    wl = W.config_workload(cfg, device=cuda_device)
+    out_d, lse_d = api.sparse_attn_sharedkv(wl.q, return_softmax_lse=True, kernel=kernel, check_status=True,
+                                            **wl.api_kwargs())
+    torch.cuda.synchronize()
+    # properties on every token, evaluated on the device (c4's out is 2^31 elements)
+    assert bool(torch.isfinite(out_d).all()) and bool(torch.isfinite(lse_d).all())
+    assert bool((lse_d >= wl.sinks[None, :] - 1e-5).all())
+
+    def absmax(t):
+        return max(abs(float(t.amax())), abs(float(t.amin())))
+
+    vmax = max(absmax(wl.ori_kv), absmax(wl.cmp_kv))
+    assert absmax(out_d) <= vmax + 1e-2
+    toks = SM.stratified_tokens(wl, per_request_prefill=3 if cfg == "c4" else None,
+                                max_requests=64 if cfg == "c5" else None)
+    sel = torch.as_tensor(toks, device=cuda_device)
+    out = out_d.index_select(0, sel).float().cpu().numpy()
+    lse = lse_d.index_select(0, sel).cpu().numpy()
+    del out_d, lse_d
+    ref_out, ref_lse = SM.oracle_tokens(wl, toks)
+    dlse = float(np.abs(lse - ref_lse).max())
+    excess = float((np.abs(out - ref_out) - (OUT_ATOL + OUT_RTOL * np.abs(ref_out))).max())
+    print(f"\n[parity] {cfg} {kernel}: {len(toks)} of {wl.num_tokens} tokens checked, max|dlse| {dlse:.2e}, "
+          f"max out excess over atol/rtol {excess:.2e}")
+    assert_close_to_golden(out, lse, ref_out, ref_lse, f"{cfg} {kernel}")
 
 
 @pytest.mark.parametrize("batch", [1, 4, 16, 37])

@@ -6,9 +6,11 @@ with no device allocator -- and cannot hand sas_forward a workspace.  For them
 sas_forward_noalloc runs the same kernels over a scratch array compiled into
 the library.  This test calls both entry points through the C ABI on the same
 inputs, twice in a row with different workloads (the scratch keeps the
-previous call's contents), and requires the same results within the parity
-tolerances of the other GPU tests.  It is collected last on purpose: a failure
-here leaves every other test already run.
+previous call's contents), and requires identical bits: both entry points run
+the same deterministic kernels on the same inputs, only the workspace differs.
+It also reads the scratch's status word back (clean after a valid call, the
+bad-index bit after a call with an index below -1).  It is collected last on
+purpose: a failure here leaves every other test already run.
 """
 
 import ctypes
@@ -21,8 +23,6 @@ from dsv4_planb_b200 import _lib
 from dsv4_planb_b200 import workloads as W
 
 pytestmark = pytest.mark.gpu
-
-OUT_ATOL, OUT_RTOL, LSE_ATOL = 2e-2, 1e-2, 1e-3
 
 
 def _args(wl):
@@ -73,8 +73,22 @@ def test_noalloc_matches_workspace_entry_point(cuda_device):
         ref_out, ref_lse = _call(lib, wl, noalloc=False)
         out, lse = _call(lib, wl, noalloc=True)
         assert np.isfinite(out).all() and np.isfinite(lse).all()
-        assert (np.abs(out - ref_out) <= OUT_ATOL + OUT_RTOL * np.abs(ref_out)).all()
-        assert np.abs(lse - ref_lse).max() <= LSE_ATOL
+        np.testing.assert_array_equal(out, ref_out)
+        np.testing.assert_array_equal(lse, ref_lse)
+        st = ctypes.c_uint32(0xFFFFFFFF)
+        assert lib.sas_noalloc_read_status(ctypes.byref(st), torch.cuda.current_stream().cuda_stream) == 0
+        assert st.value == 0
+
+
+def test_noalloc_status_word_reports_bad_indices(cuda_device):
+    lib = _lib.load()
+    wl = W.make_workload(name="na4", q_lens=[1, 1], kv_lens=[900, 900], num_heads=128, topk=64, device=cuda_device,
+                         index_method="keys")
+    wl.cmp_sparse_indices[0, 0, 3] = -5  # below -1: skipped, and the status word says so
+    _call(lib, wl, noalloc=True)
+    st = ctypes.c_uint32(0)
+    assert lib.sas_noalloc_read_status(ctypes.byref(st), torch.cuda.current_stream().cuda_stream) == 0
+    assert st.value & _lib.SAS_STATUS_BAD_INDEX
 
 
 def test_noalloc_rejects_oversized_calls(cuda_device):
