@@ -32,6 +32,7 @@ SAS_DTYPE_FP16 = 1
 
 SAS_FWD_FLAG_CU_SEQLENS = 0x1
 SAS_FWD_FLAG_TEST_STALL = 0x100
+SAS_FWD_FLAG_LAZY_RESCALE = 0x200
 
 KERNELS = {"auto": 0, "simt": 1, "tc": 2}
 LAYOUT_Q = {"BSND": 0, "BSH": 1, "TND": 2}
@@ -45,6 +46,8 @@ EXPORTS = (
     "sas_forward_noalloc",
     "sas_noalloc_read_status",
     "sas_resolve_rows",
+    "sas_split_plan",
+    "sas_split_metadata",
     "sas_read_status",
     "sas_set_kernel_events",
     "sas_metadata_workspace_size",
@@ -125,6 +128,9 @@ _SIGNATURES = {
     "sas_forward_noalloc": (ctypes.c_int, [ctypes.POINTER(SasFwdArgs)] + [_P] * 13 + [_P]),
     "sas_noalloc_read_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), _P]),
     "sas_resolve_rows": (ctypes.c_int, [ctypes.POINTER(SasFwdArgs)] + [_P] * 8 + [_P, _SZ, _P]),
+    "sas_split_plan": (ctypes.c_int, [ctypes.POINTER(SasFwdArgs), ctypes.POINTER(ctypes.c_int32),
+                                      ctypes.POINTER(ctypes.c_int32)]),
+    "sas_split_metadata": (ctypes.c_int, [ctypes.POINTER(SasFwdArgs)] + [_P] * 7 + [_P, _SZ, _P]),
     "sas_read_status": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_uint32), _P]),
     "sas_set_kernel_events": (ctypes.c_int, [_P, _P]),
     "sas_metadata_workspace_size": (ctypes.c_int, [ctypes.POINTER(SasMetaArgs), ctypes.POINTER(_SZ)]),

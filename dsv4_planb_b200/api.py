@@ -26,8 +26,8 @@ Differences, all widenings of the reference contract:
   on the host, api.py:260), and TND needs none once ``max_seqlen_q`` is given;
 * extra keywords ``kernel`` ("auto" | "simt" | "tc"), ``max_seqlen_q`` (skips
   the host read of ``cu_seqlens_q``), ``out`` / ``lse_out`` (preallocated
-  outputs), ``check_status`` (read the device status word, synchronising) and
-  ``split_tiles``.
+  outputs), ``check_status`` (read the device status word, synchronising),
+  ``split_tiles`` and ``lazy_rescale``.
 """
 
 from __future__ import annotations
@@ -97,7 +97,7 @@ def _out_shapes(q: torch.Tensor, layout_q: str, v_head_dim: int):
 
 def _launch(q, ori_kv, cmp_kv, cmp_sparse_indices, ori_block_table, cmp_block_table, cu_seqlens_q, seqused_kv,
             sinks, metadata, softmax_scale, cmp_ratio, ori_win_left, layout_q, v_head_dim, kernel, max_seqlen_q,
-            split_tiles, check_status, out, lse_out):
+            split_tiles, check_status, lazy_rescale, out, lse_out):
     """Marshal one sas_forward call (the body of both registered ops).  ``out`` / ``lse_out`` are the
     outputs in the layout of ``q``; ``max_seqlen_q`` < 0 reads it from ``cu_seqlens_q`` (host sync)."""
     dev = q.device
@@ -180,7 +180,8 @@ def _launch(q, ori_kv, cmp_kv, cmp_sparse_indices, ori_block_table, cmp_block_ta
     args.dtype = _dtype_code(q.dtype)
     args.softmax_scale = float(softmax_scale)
     args.kernel = _lib.KERNELS[kernel]
-    args.flags = _lib.SAS_FWD_FLAG_CU_SEQLENS if layout_q == "TND" else 0
+    args.flags = (_lib.SAS_FWD_FLAG_CU_SEQLENS if layout_q == "TND" else 0) | (
+        _lib.SAS_FWD_FLAG_LAZY_RESCALE if lazy_rescale else 0)
     args.split_tiles = int(split_tiles)
 
     lib = _lib.load()
@@ -229,21 +230,21 @@ def _op(q: torch.Tensor, ori_kv: torch.Tensor, cmp_kv: Optional[torch.Tensor],
         cmp_block_table: Optional[torch.Tensor], cu_seqlens_q: Optional[torch.Tensor], seqused_kv: torch.Tensor,
         sinks: torch.Tensor, metadata: Optional[torch.Tensor], softmax_scale: float, cmp_ratio: int,
         ori_win_left: int, layout_q: str, v_head_dim: int, kernel: str, max_seqlen_q: int, split_tiles: int,
-        check_status: bool) -> Tuple[torch.Tensor, torch.Tensor]:
+        check_status: bool, lazy_rescale: bool) -> Tuple[torch.Tensor, torch.Tensor]:
     """sparse_attn_sharedkv with op-owned outputs: returns ``(out, lse)`` in the layout of ``q``."""
     o_shape, l_shape = _out_shapes(q, layout_q, v_head_dim)
     out = torch.empty(o_shape, dtype=q.dtype, device=q.device)
     lse = torch.empty(l_shape, dtype=torch.float32, device=q.device)
     _launch(q, ori_kv, cmp_kv, cmp_sparse_indices, ori_block_table, cmp_block_table, cu_seqlens_q, seqused_kv,
             sinks, metadata, softmax_scale, cmp_ratio, ori_win_left, layout_q, v_head_dim, kernel, max_seqlen_q,
-            split_tiles, check_status, out, lse)
+            split_tiles, check_status, lazy_rescale, out, lse)
     return out, lse
 
 
 @_op.register_fake
 def _op_fake(q, ori_kv, cmp_kv, cmp_sparse_indices, ori_block_table, cmp_block_table, cu_seqlens_q, seqused_kv,
              sinks, metadata, softmax_scale, cmp_ratio, ori_win_left, layout_q, v_head_dim, kernel, max_seqlen_q,
-             split_tiles, check_status):
+             split_tiles, check_status, lazy_rescale):
     o_shape, l_shape = _out_shapes(q, layout_q, v_head_dim)
     return q.new_empty(o_shape), q.new_empty(l_shape, dtype=torch.float32)
 
@@ -254,17 +255,17 @@ def _op_out(q: torch.Tensor, ori_kv: torch.Tensor, cmp_kv: Optional[torch.Tensor
             cmp_block_table: Optional[torch.Tensor], cu_seqlens_q: Optional[torch.Tensor], seqused_kv: torch.Tensor,
             sinks: torch.Tensor, metadata: Optional[torch.Tensor], softmax_scale: float, cmp_ratio: int,
             ori_win_left: int, layout_q: str, v_head_dim: int, kernel: str, max_seqlen_q: int, split_tiles: int,
-            check_status: bool, out: torch.Tensor, lse: torch.Tensor) -> None:
+            check_status: bool, lazy_rescale: bool, out: torch.Tensor, lse: torch.Tensor) -> None:
     """sparse_attn_sharedkv into caller-owned ``out`` / ``lse`` (layout of ``q``)."""
     _launch(q, ori_kv, cmp_kv, cmp_sparse_indices, ori_block_table, cmp_block_table, cu_seqlens_q, seqused_kv,
             sinks, metadata, softmax_scale, cmp_ratio, ori_win_left, layout_q, v_head_dim, kernel, max_seqlen_q,
-            split_tiles, check_status, out, lse)
+            split_tiles, check_status, lazy_rescale, out, lse)
 
 
 @_op_out.register_fake
 def _op_out_fake(q, ori_kv, cmp_kv, cmp_sparse_indices, ori_block_table, cmp_block_table, cu_seqlens_q, seqused_kv,
                  sinks, metadata, softmax_scale, cmp_ratio, ori_win_left, layout_q, v_head_dim, kernel, max_seqlen_q,
-                 split_tiles, check_status, out, lse):
+                 split_tiles, check_status, lazy_rescale, out, lse):
     return None
 
 
@@ -299,6 +300,7 @@ def sparse_attn_sharedkv(
     lse_out: Optional[torch.Tensor] = None,
     check_status: bool = False,
     split_tiles: int = 0,
+    lazy_rescale: bool = False,
 ) -> Union[torch.Tensor, Tuple[torch.Tensor, torch.Tensor]]:
     """Sink-seeded sliding-window + compressed attention over a shared K = V cache.
 
@@ -312,7 +314,9 @@ def sparse_attn_sharedkv(
     ``max_seqlen_q`` (no host synchronisation when given), ``out`` / ``lse_out``
     (caller-owned outputs), ``check_status`` (raise on device-side status bits) and
     ``split_tiles`` (piece size, in 64-key tiles, for cutting long tokens across the
-    tensor-core path's clusters; 0 lets the library decide; see ``sharding.split_hint``).
+    tensor-core path's clusters; 0 lets the library decide; see ``sharding.split_hint``) and
+    ``lazy_rescale`` (``SAS_FWD_FLAG_LAZY_RESCALE``: raise the softmax's running max only past a
+    threshold, faster, P rounded at another scale than the golden's; off by default).
     Everything here is shape logic that ``torch.compile`` traces; the launch is the
     registered op ``torch.ops.sas_b200.sparse_attn_sharedkv`` (``..._out`` with ``out``).
     """
@@ -350,7 +354,7 @@ def sparse_attn_sharedkv(
     mq = -1 if max_seqlen_q is None else int(max_seqlen_q)
     common = (q, ori_kv, cmp_kv, cmp_sparse_indices, ori_block_table, cmp_block_table, cu_seqlens_q, seqused_kv,
               sinks, metadata, float(softmax_scale), ratio, int(ori_win_left), layout_q, Dv, kernel, mq,
-              int(split_tiles), bool(check_status))
+              int(split_tiles), bool(check_status), bool(lazy_rescale))
     if out is None and lse_out is None:
         out_r, lse_r = torch.ops.sas_b200.sparse_attn_sharedkv(*common)
     else:
@@ -423,3 +427,66 @@ def resolve_rows(
     st = _lib.ctypes.c_uint32(0)
     _lib.check(lib.sas_read_status(_ptr(ws), _lib.ctypes.byref(st), stream), "sas_read_status")
     return tinfo, rows[:, :cap], st.value
+
+
+def split_plan(args) -> Tuple[int, int]:
+    """``(pieces, tiles_per_piece)`` of the split-KV plan ``sas_forward`` runs for ``args`` (an
+    ``_lib.SasFwdArgs``); ``(1, 0)``: whole tokens."""
+    lib = _lib.load()
+    p, m = _lib.ctypes.c_int32(0), _lib.ctypes.c_int32(0)
+    _lib.check(lib.sas_split_plan(_lib.ctypes.byref(args), _lib.ctypes.byref(p), _lib.ctypes.byref(m)),
+               "sas_split_plan")
+    return p.value, m.value
+
+
+def split_metadata(
+    *,
+    cmp_sparse_indices: torch.Tensor,
+    ori_block_table: torch.Tensor,
+    cmp_block_table: torch.Tensor,
+    cu_seqlens_q: torch.Tensor,
+    seqused_kv: torch.Tensor,
+    num_heads: int,
+    head_dim: int,
+    v_head_dim: int,
+    ori_block_num: int,
+    ori_block_size: int,
+    cmp_block_num: int,
+    cmp_block_size: int,
+    cmp_ratio: int = 4,
+    ori_win_left: int = 127,
+    split_tiles: int = 0,
+    max_seqlen_q: Optional[int] = None,
+    kernel: str = "auto",
+):
+    """The tensor-core path's split-KV plan for a TND SCFA call, as ``int32[1024]`` in the reference
+    metadata layout (FD rows, ``sas_split_metadata``), plus the ``SasFwdArgs`` it was planned for."""
+    dev = ori_block_table.device
+    cu = _i32(cu_seqlens_q, dev)
+    B = cu.numel() - 1
+    T = cmp_sparse_indices.shape[0]
+    if max_seqlen_q is None:
+        cu_h = cu_seqlens_q.detach().to("cpu", torch.int64)
+        max_seqlen_q = int((cu_h[1:] - cu_h[:-1]).max().item()) if B > 0 else 0
+    args = _lib.SasFwdArgs()
+    args.batch, args.num_tokens, args.max_q_len = B, T, int(max_seqlen_q)
+    args.num_heads, args.num_kv_heads, args.head_dim, args.v_head_dim = num_heads, 1, head_dim, v_head_dim
+    args.ori_block_num, args.ori_block_size, args.ori_table_len = ori_block_num, ori_block_size, ori_block_table.shape[1]
+    args.cmp_block_num, args.cmp_block_size, args.cmp_table_len = cmp_block_num, cmp_block_size, cmp_block_table.shape[1]
+    args.topk, args.cmp_ratio, args.scenario = cmp_sparse_indices.shape[-1], cmp_ratio, 3
+    args.ori_win_left, args.ori_mask_mode, args.cmp_mask_mode = ori_win_left, 4, 3
+    args.dtype, args.softmax_scale, args.kernel = _lib.SAS_DTYPE_BF16, 1.0, _lib.KERNELS[kernel]
+    args.flags = _lib.SAS_FWD_FLAG_CU_SEQLENS
+    args.split_tiles = int(split_tiles)
+    lib = _lib.load()
+    nbytes = _lib.ctypes.c_size_t(0)
+    _lib.check(lib.sas_workspace_size(_lib.ctypes.byref(args), _lib.ctypes.byref(nbytes)), "sas_workspace_size")
+    ws = _workspace(nbytes.value, dev)
+    out = torch.empty(SAS_META_SIZE, dtype=torch.int32, device=dev)
+    idx = _i32(cmp_sparse_indices, dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    rc = lib.sas_split_metadata(_lib.ctypes.byref(args), _ptr(_i32(ori_block_table, dev)),
+                                _ptr(_i32(cmp_block_table, dev)), _ptr(idx), _ptr(cu), None,
+                                _ptr(_i32(seqused_kv, dev)), _ptr(out), _ptr(ws), ws.numel(), stream)
+    _lib.check(rc, "sas_split_metadata")
+    return out, args

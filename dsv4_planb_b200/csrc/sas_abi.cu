@@ -22,6 +22,9 @@ int launch_fwd_simt(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, cons
 bool tc_supported(const SasFwdArgs &a);
 size_t tc_workspace(const SasFwdArgs &a);
 int tc_kernel_count(const SasFwdArgs &a);
+void tc_split_shape(const SasFwdArgs &a, int32_t *pieces, int32_t *tiles);
+int launch_split_metadata(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, bool tc, int32_t *out,
+                          cudaStream_t s);
 int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const void *q, const void *ori_kv,
                   const int32_t *ori_bt, const void *cmp_kv, const int32_t *cmp_bt, const float *sinks, void *out,
                   float *lse, cudaStream_t s);
@@ -53,7 +56,8 @@ int validate_fwd(const SasFwdArgs &a) {
     if (a.scenario == 3 && a.topk < 0) return SAS_ERR_INVALID_ARG;
     if (a.scenario == 2 && a.max_cmp_len < 0) return SAS_ERR_INVALID_ARG;
     if (a.kernel < SAS_KERNEL_AUTO || a.kernel > SAS_KERNEL_TC) return SAS_ERR_INVALID_ARG;
-    if ((a.flags & ~(SAS_FWD_FLAG_CU_SEQLENS | SAS_FWD_FLAG_TEST_STALL)) != 0) return SAS_ERR_INVALID_ARG;
+    if ((a.flags & ~(SAS_FWD_FLAG_CU_SEQLENS | SAS_FWD_FLAG_TEST_STALL | SAS_FWD_FLAG_LAZY_RESCALE)) != 0)
+        return SAS_ERR_INVALID_ARG;
     if (a.split_tiles < 0) return SAS_ERR_INVALID_ARG;
     for (int i = 0; i < 4; ++i)
         if (a.reserved[i] != 0) return SAS_ERR_INVALID_ARG;
@@ -231,6 +235,42 @@ int sas_resolve_rows(const SasFwdArgs *args, const int32_t *ori_block_table, con
                                    cudaMemcpyDeviceToDevice, s)))
         return SAS_ERR_CUDA;
     return SAS_OK;
+}
+
+int sas_split_plan(const SasFwdArgs *args, int32_t *pieces, int32_t *tiles_per_piece) {
+    if (!args || !pieces || !tiles_per_piece) return SAS_ERR_INVALID_ARG;
+    const int rc = validate_fwd(*args);
+    if (rc) return rc;
+    if (use_tc(*args)) {
+        tc_split_shape(*args, pieces, tiles_per_piece);
+    } else {
+        *pieces = 1;
+        *tiles_per_piece = 0;
+    }
+    return SAS_OK;
+}
+
+int sas_split_metadata(const SasFwdArgs *args, const int32_t *ori_block_table, const int32_t *cmp_block_table,
+                       const int32_t *cmp_indices, const int32_t *q_prefix, const int32_t *act_q_len,
+                       const int32_t *act_kv_len, int32_t *metadata_out, void *workspace, size_t workspace_bytes,
+                       void *stream) {
+    if (!args || !metadata_out) return SAS_ERR_INVALID_ARG;
+    const SasFwdArgs &a = *args;
+    int rc = validate_fwd(a);
+    if (rc) return rc;
+    rc = check_inputs(a, ori_block_table, ori_block_table, cmp_block_table, cmp_block_table, cmp_indices, q_prefix,
+                      act_q_len, act_kv_len);
+    if (rc) return rc;
+    const sas::FwdLayout L = fwd_layout(a);
+    if (!workspace || workspace_bytes < L.total) return SAS_ERR_WORKSPACE;
+    rc = check_alignment(nullptr, nullptr, ori_block_table, nullptr, cmp_block_table, cmp_indices, q_prefix,
+                         act_q_len, act_kv_len, nullptr, nullptr, nullptr, workspace);
+    if (rc || !aligned(metadata_out, 4)) return SAS_ERR_INVALID_ARG;
+    char *ws = static_cast<char *>(workspace);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    rc = launch_prep(a, L, ws, cmp_block_table, cmp_indices, q_prefix, act_q_len, act_kv_len, s);
+    if (rc) return rc;
+    return launch_split_metadata(a, L, ws, use_tc(a), metadata_out, s);
 }
 
 int sas_read_status(const void *workspace, uint32_t *status, void *stream) {

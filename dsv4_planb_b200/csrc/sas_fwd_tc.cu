@@ -25,11 +25,12 @@
 // Keys of a token are its window rows (padded to a multiple of 64) followed by
 // its resolved compressed rows (sas_prep.cu); masked / unmapped rows are read
 // as zeros (the gather points them past the pool).  Scores live in the
-// log2 domain.  The running max follows every increase (P <= 1), so P is
-// rounded to bf16 at the scale of the exact running max, as the reference
-// golden rounds it (golden.py:186-194); the output CTA rescales the rows of O
-// whose max rose.  The final out = O / lr and lse = (m + log2 l) ln 2 equal
-// the golden up to rounding.
+// log2 domain.  By default the running max follows every increase (P <= 1),
+// so P is rounded to bf16 at the scale of the exact running max, as the
+// reference golden rounds it (golden.py:186-194); the output CTA rescales the
+// rows of O whose max rose (SAS_FWD_FLAG_LAZY_RESCALE raises it only past a
+// threshold).  The final out = O / lr and lse = (m + log2 l) ln 2 equal the
+// golden up to rounding.
 //
 // Every wait is bounded by %globaltimer; a timeout sets SAS_STATUS_WAIT_TIMEOUT,
 // raises an abort flag in both CTAs and lets every role fall through to the
@@ -56,13 +57,16 @@ constexpr int kThreads = 288;       // warps 0-3 softmax / epilogue, 4-7 gather,
 constexpr int kChunkBytes = kBK * 128;  // one 64-column slab of a 64-row tile (128B-swizzled)
 constexpr int kMaxDq = 576;
 constexpr int kMaxDv = 512;
-// Rescale threshold of the running max (log2 units): 0 = raise it on every increase.  A lazy
-// threshold (FlashAttention-4 style; 8 keeps P <= 256) rescales O less often, but rounds P to bf16
-// at another scale than the reference golden, whose P have a row maximum of exactly 1: with 8, the
-// reference paramsets' low-precision acceptance (>= 99.5 % of elements within bf16 rtol 2^-7 of the
-// golden's bf16 output) fell to 99.18-99.67 %; with 0 it is 99.84-99.96 % (CPU emulation of this
-// kernel's arithmetic on the reference paramsets).
-constexpr float kTau = 0.0f;
+// Rescale threshold of the running max (log2 units), per launch.  Default 0: the max follows every
+// increase (P <= 1), so P is rounded to bf16 at the scale the reference golden rounds it
+// (golden.py:186-194, whose row maximum is exactly 1) and the output CTA rescales the rows of O
+// whose max rose.  SAS_FWD_FLAG_LAZY_RESCALE: 8 (FlashAttention-4 style; P <= 256), so O is rarely
+// rescaled; P is then rounded at another scale than the golden's.  Measured by CPU emulation of this
+// kernel's arithmetic on the reference paramsets, the share of elements within the reference's own
+// acceptance (bf16 rtol 2^-7 of the golden's bf16 output, >= 99.5 % required) is 99.84-99.96 % with
+// 0, 99.58-99.87 % with 0.25 and 99.18-99.67 % with 8; on B200 the lazy threshold makes the c2
+// decode kernel ~15 % faster.  Both meet the north-star bars against the fp32 golden.
+constexpr float kTauLazy = 8.0f;
 constexpr uint64_t kTimeoutNs = 4000000000ull;
 
 // P message: bf16 P [128 heads][64 keys] (SW128 K-major) + per-head floats.
@@ -157,6 +161,7 @@ struct TcArgs {
     int test_stall;          // SAS_FWD_FLAG_TEST_STALL: withhold the first P-slot release
     int *counter;            // next unit to hand out (zeroed with the status word before the launch)
     float scale_log2;
+    float tau;               // rescale threshold of the running max (log2 units)
     // Split KV: token t's tiles are cut into pieces of M tiles; unit u is piece u / T of token
     // u % T (U = T * P units).  P = 1: one unit per token.  Every piece of a token cut into
     // np > 1 pieces leaves o = O / lr (bf16) and (m, l, lr) in slot (t, piece); combine_kernel
@@ -725,7 +730,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         l *= a0;
                         lr *= a0;
                         m = mn;
-                    } else if (mx > m + kTau) {
+                    } else if (mx > m + p.tau) {
                         alpha = exp2f(m - mx);
                         l *= alpha;
                         lr *= alpha;
@@ -1043,6 +1048,68 @@ __global__ void __launch_bounds__(kMaxDv / 8) combine_kernel(const TcArgs p) {
     *reinterpret_cast<uint4 *>(out) = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// The split-KV plan of a launch in the reference's metadata layout (metadata.py:38-60, 974-1009):
+// FA rows stay zero (clusters take units from a dynamic queue, not static ranges); FD row i (at
+// int 288 + 8 i) describes the i-th token, in token order, that the attention kernel cuts into
+// np > 1 pieces: {1, b, s, t * P, np, 0, N1, 0}.  Int 864 holds the number of such tokens (rows
+// past the 72nd are not listed).  One CTA; the tokens are ranked by a block-wide scan.
+__global__ void __launch_bounds__(1024) split_metadata_kernel(const int32_t *tinfo, int T, int P, int M, int N1,
+                                                              int32_t *out) {
+    __shared__ int warp_sums[32];
+    __shared__ int base_s;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int i = tid; i < 1024; i += blockDim.x) out[i] = 0;
+    if (tid == 0) base_s = 0;
+    __syncthreads();
+    for (int t0 = 0; t0 < T; t0 += blockDim.x) {
+        const int t = t0 + tid;
+        int np = 1, b = 0, s = 0;
+        if (t < T) {
+            const int32_t *ti = tinfo + (int64_t)t * sas::TI_INTS;
+            const int nwt = (ti[sas::TI_NWIN] + kBK - 1) / kBK;
+            const int ntiles = ti[sas::TI_VALID] ? nwt + (ti[sas::TI_NCMP] + kBK - 1) / kBK : 0;
+            np = P > 1 && ntiles > M ? min((ntiles + M - 1) / M, P) : 1;  // as load_unit cuts it
+            b = ti[sas::TI_B];
+            s = ti[sas::TI_S];
+        }
+        const int flag = np > 1 ? 1 : 0;
+        int x = flag;  // block-wide inclusive scan of the split flags
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        if (lane == 31) warp_sums[warp] = x;
+        __syncthreads();
+        if (warp == 0) {
+            int w = lane < (int)(blockDim.x >> 5) ? warp_sums[lane] : 0;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, w, o);
+                if (lane >= o) w += y;
+            }
+            warp_sums[lane] = w;
+        }
+        __syncthreads();
+        const int rank = base_s + (warp > 0 ? warp_sums[warp - 1] : 0) + x - flag;
+        if (flag && rank < 72) {
+            int32_t *row = out + 288 + 8 * rank;
+            row[0] = 1;
+            row[1] = b;
+            row[2] = s;
+            row[3] = t * P;
+            row[4] = np;
+            row[5] = 0;
+            row[6] = N1;
+            row[7] = 0;
+        }
+        __syncthreads();
+        if (tid == 0) base_s += warp_sums[(blockDim.x >> 5) - 1];
+        __syncthreads();
+    }
+    if (tid == 0) out[864] = base_s;
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -1141,6 +1208,20 @@ size_t part_o_bytes(const SasFwdArgs &a, const SplitPlan &sp) {
 
 int tc_kernel_count(const SasFwdArgs &a) { return split_plan(a).P > 1 ? 2 : 1; }
 
+void tc_split_shape(const SasFwdArgs &a, int32_t *pieces, int32_t *tiles) {
+    const SplitPlan sp = split_plan(a);
+    *pieces = sp.P;
+    *tiles = sp.P > 1 ? sp.M : 0;
+}
+
+int launch_split_metadata(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, bool tc, int32_t *out,
+                          cudaStream_t s) {
+    const SplitPlan sp = tc ? split_plan(a) : SplitPlan{1, 0};
+    split_metadata_kernel<<<1, 1024, 0, s>>>(reinterpret_cast<const int32_t *>(ws + L.token_info), a.num_tokens,
+                                             sp.P, sp.M, a.num_heads, out);
+    return check_cuda(cudaGetLastError());
+}
+
 size_t tc_workspace(const SasFwdArgs &a) {
     const SplitPlan sp = split_plan(a);
     if (sp.P <= 1) return 0;
@@ -1179,6 +1260,7 @@ int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const 
     p.ori_rows = a.ori_block_num * a.ori_block_size;
     p.cmp_rows = a.scenario >= 2 ? a.cmp_block_num * a.cmp_block_size : p.ori_rows;
     p.scale_log2 = a.softmax_scale * 1.4426950408889634f;
+    p.tau = (a.flags & SAS_FWD_FLAG_LAZY_RESCALE) ? kTauLazy : 0.f;
     p.test_stall = (a.flags & SAS_FWD_FLAG_TEST_STALL) ? 1 : 0;
     p.counter = reinterpret_cast<int *>(ws + L.status + sas::kTokenCounterOff);
     const SplitPlan sp = split_plan(a);

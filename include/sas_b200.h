@@ -113,6 +113,19 @@ typedef struct SasFwdArgs {
  * Nothing faults, traps or spins without bound.
  */
 #define SAS_FWD_FLAG_TEST_STALL 0x100
+/*
+ * SAS_FWD_FLAG_LAZY_RESCALE: performance mode of the tensor-core kernel.  By
+ * default its online softmax raises the running max on every increase, so P
+ * is rounded to bf16 / fp16 at the scale the reference golden rounds it
+ * (golden.py:186-194) and the reference's own low-precision acceptance
+ * (test_sparse_attn_sharedkv.py:394-467) holds.  With this flag the max is
+ * raised only when it grows by more than 8 (log2 units), so the 128 x 512
+ * fp32 O accumulator is rarely rescaled (about 15 % faster at the c2 decode
+ * shape); P is then rounded at another scale, and results stay within the
+ * north-star bars against the fp32 golden.  Ignored by the CUDA-core kernel.
+ * No counterpart in the reference.
+ */
+#define SAS_FWD_FLAG_LAZY_RESCALE 0x200
 
 /* Bytes of workspace sas_forward needs for `args` (256-byte aligned base). */
 int sas_workspace_size(const SasFwdArgs *args, size_t *bytes);
@@ -169,6 +182,43 @@ int sas_resolve_rows(const SasFwdArgs *args, const int32_t *ori_block_table, con
                      const int32_t *cmp_indices, const int32_t *q_prefix, const int32_t *act_q_len,
                      const int32_t *act_kv_len, int32_t *token_info, int32_t *cmp_rows, void *workspace,
                      size_t workspace_bytes, void *stream);
+
+/*
+ * Shape of the split-KV plan sas_forward would run for `args` (host only, no
+ * device work): the tensor-core path cuts every token of more than
+ * *tiles_per_piece tiles of 64 keys into at most *pieces pieces; *pieces == 1
+ * (and *tiles_per_piece == 0) means whole tokens.  The workspace then holds
+ * partials for T x pieces slots: bf16 out [T][pieces][N1][D_v] and fp32
+ * (m, l, lr, 0) [T][pieces][N1][4].  No counterpart in the reference.
+ */
+int sas_split_plan(const SasFwdArgs *args, int32_t *pieces, int32_t *tiles_per_piece);
+
+/*
+ * The split-KV plan of one sas_forward call with the same arguments, written to
+ * metadata_out (device int32[1024]) in the layout of the reference's metadata
+ * (metadata.py:38-60, packed at metadata.py:974-1009).  It completes what the
+ * reference's scheduler declares but never enables (supportFd = False,
+ * metadata.py:323-325; FD bookkeeping metadata.py:795-827, 925-954):
+ *   - FA rows (ints 0..287): all zero.  The B200 kernel's 74 two-SM clusters take
+ *     units (whole tokens, or pieces of split tokens) from a dynamic queue, so
+ *     there is no static per-core range to describe.
+ *   - FD row i (ints 288 + 8i .. +7, i < 72): the i-th token, in flat-row order,
+ *     that the tensor-core kernel cuts into np > 1 pieces:
+ *     {enable 1, bn2 = b (one KV head), m = s (query index in its request; the
+ *     reference's mBaseSize is the group size, so its s1g index is s), ws_idx =
+ *     t * pieces (first slot of the token in the partial buffers), ws_num = np,
+ *     m_start = 0, m_num = N1 (the combine merges every head of the token), 0}.
+ *     The Ascend meaning differs in m_start / m_num, which there split one
+ *     token's heads across vector cores.
+ *   - int 864 (zero in the reference): how many tokens are split; rows past the
+ *     72nd are not listed.
+ * Runs the key resolution (like sas_resolve_rows) into `workspace` (sized by
+ * sas_workspace_size), then one small kernel.  No host synchronisation.
+ */
+int sas_split_metadata(const SasFwdArgs *args, const int32_t *ori_block_table, const int32_t *cmp_block_table,
+                       const int32_t *cmp_indices, const int32_t *q_prefix, const int32_t *act_q_len,
+                       const int32_t *act_kv_len, int32_t *metadata_out, void *workspace, size_t workspace_bytes,
+                       void *stream);
 
 /*
  * Reads the device status word a previous call on `workspace` left behind

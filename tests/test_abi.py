@@ -272,10 +272,41 @@ def test_registered_op_fake_shapes():
         kv = torch.empty(2, dtype=torch.int32)
         sinks = torch.empty(128, dtype=torch.float32)
         out, lse = torch.ops.sas_b200.sparse_attn_sharedkv(q, pool, pool, idx, bt, bt, cu, kv, sinks, None, 0.04, 4,
-                                                           127, "TND", 512, "auto", 3, 0, False)
+                                                           127, "TND", 512, "auto", 3, 0, False, False)
         assert out.shape == (6, 128, 512) and out.dtype == torch.bfloat16
         assert lse.shape == (6, 128) and lse.dtype == torch.float32
         qb = torch.empty(2, 3, 128, 576, dtype=torch.bfloat16)
         out, lse = torch.ops.sas_b200.sparse_attn_sharedkv(qb, pool, None, None, bt, None, None, kv, sinks, None,
-                                                           0.04, 4, 127, "BSND", 512, "tc", -1, 0, False)
+                                                           0.04, 4, 127, "BSND", 512, "tc", -1, 0, False, True)
         assert out.shape == (2, 3, 128, 512) and lse.shape == (2, 3, 128)
+
+
+def test_split_plan_shape_matches_the_workspace(lib):
+    # The plan sas_split_plan reports is the one sas_workspace_size sizes: bf16 partial outputs and
+    # fp32 (m, l, lr, 0) statistics for T x pieces slots.  Small SCFA batches on the tensor-core path
+    # split; large ones, the CUDA-core kernel and a caller's piece size >= a token's tiles do not.
+    def plan(a):
+        p, m = ctypes.c_int32(-1), ctypes.c_int32(-1)
+        assert lib.sas_split_plan(ctypes.byref(a), ctypes.byref(p), ctypes.byref(m)) == 0
+        return p.value, m.value
+
+    for T in (1, 4, 16, 37, 38, 64):
+        a = good_args()
+        a.batch, a.num_tokens, a.max_q_len = T, T, 1
+        a.num_heads, a.head_dim, a.v_head_dim, a.topk, a.kernel = 128, 576, 512, 2048, 0
+        P, M = plan(a)
+        if T <= 37:
+            assert P > 1 and M >= 4 and P * M >= 34 and (P - 1) * M < 34, (T, P, M)
+        else:
+            assert (P, M) == (1, 0)
+        base = ws_size(lib, a)[1]
+        a.kernel = _lib.KERNELS["simt"]
+        assert plan(a) == (1, 0)
+        simt = ws_size(lib, a)[1]
+        assert base - simt >= (T * P * 128 * (512 * 2 + 16) if P > 1 else 0)
+        assert base - simt < (T * P * 128 * (512 * 2 + 16) if P > 1 else 0) + 512
+        a.kernel, a.split_tiles = 0, 40  # a piece size no token exceeds: whole tokens
+        assert plan(a) == (1, 0)
+        a.split_tiles = 6
+        P, M = plan(a)
+        assert M == 6 and P == -(-34 // 6)
