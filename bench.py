@@ -69,7 +69,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
-    ap.add_argument("--kernel", default="auto", choices=["auto", "simt", "tc"])
+    ap.add_argument("--kernel", default="auto", choices=["auto", "simt", "tc", "tc2"])
     ap.add_argument("--batch", type=int, default=None,
                     help="request count of c2 / c3 (default 64 / 32): small-batch decode measurements")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -712,7 +712,7 @@ def main():
     k_avg_ms = statistics.mean(kernel_ms)
     achieved = figs["bytes"] / (k_avg_ms / 1e3) / 1e9
     tflops = figs["flops"] / (k_avg_ms / 1e3) / 1e12
-    kname = "sas_fwd_tc" if tc_used(wl, args.kernel) else "fwd_simt_kernel"
+    kname = ("sas_fwd_tc2" if args.kernel == "tc2" else "sas_fwd_tc") if tc_used(wl, args.kernel) else "fwd_simt_kernel"
     if args.workload == "c4":
         # prefill is quoted as tensor-core throughput against the dense bf16 peak (burst figure:
         # the kernel holds the SM clock at its maximum, well under the power cap)

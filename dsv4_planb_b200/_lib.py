@@ -34,7 +34,7 @@ SAS_FWD_FLAG_CU_SEQLENS = 0x1
 SAS_FWD_FLAG_TEST_STALL = 0x100
 SAS_FWD_FLAG_LAZY_RESCALE = 0x200
 
-KERNELS = {"auto": 0, "simt": 1, "tc": 2}
+KERNELS = {"auto": 0, "simt": 1, "tc": 2, "tc2": 3}
 LAYOUT_Q = {"BSND": 0, "BSH": 1, "TND": 2}
 LAYOUT_KV = {"PA_ND": 0, "TND": 1}
 

@@ -27,7 +27,7 @@ int launch_split_metadata(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws
                           cudaStream_t s);
 int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const void *q, const void *ori_kv,
                   const int32_t *ori_bt, const void *cmp_kv, const int32_t *cmp_bt, const float *sinks, void *out,
-                  float *lse, cudaStream_t s);
+                  float *lse, cudaStream_t s, bool pair);
 
 int check_cuda(cudaError_t e) {
     if (e == cudaSuccess) return SAS_OK;
@@ -55,13 +55,13 @@ int validate_fwd(const SasFwdArgs &a) {
     }
     if (a.scenario == 3 && a.topk < 0) return SAS_ERR_INVALID_ARG;
     if (a.scenario == 2 && a.max_cmp_len < 0) return SAS_ERR_INVALID_ARG;
-    if (a.kernel < SAS_KERNEL_AUTO || a.kernel > SAS_KERNEL_TC) return SAS_ERR_INVALID_ARG;
+    if (a.kernel < SAS_KERNEL_AUTO || a.kernel > SAS_KERNEL_TC2) return SAS_ERR_INVALID_ARG;
     if ((a.flags & ~(SAS_FWD_FLAG_CU_SEQLENS | SAS_FWD_FLAG_TEST_STALL | SAS_FWD_FLAG_LAZY_RESCALE)) != 0)
         return SAS_ERR_INVALID_ARG;
     if (a.split_tiles < 0) return SAS_ERR_INVALID_ARG;
     for (int i = 0; i < 4; ++i)
         if (a.reserved[i] != 0) return SAS_ERR_INVALID_ARG;
-    if (a.kernel == SAS_KERNEL_TC && !tc_supported(a)) return SAS_ERR_UNSUPPORTED;
+    if ((a.kernel == SAS_KERNEL_TC || a.kernel == SAS_KERNEL_TC2) && !tc_supported(a)) return SAS_ERR_UNSUPPORTED;
     return SAS_OK;
 }
 
@@ -192,7 +192,8 @@ int sas_forward(const SasFwdArgs *args, const void *q, const void *ori_kv, const
     rc = launch_prep(a, L, ws, cmp_block_table, cmp_indices, q_prefix, act_q_len, act_kv_len, s);
     if (rc) return rc;
     if ((rc = record_kernel_event(true, s))) return rc;
-    if (use_tc(a)) rc = launch_fwd_tc(a, L, ws, q, ori_kv, ori_block_table, cmp_kv, cmp_block_table, sinks, out, lse, s);
+    if (use_tc(a)) rc = launch_fwd_tc(a, L, ws, q, ori_kv, ori_block_table, cmp_kv, cmp_block_table, sinks, out, lse, s,
+                                     a.kernel == SAS_KERNEL_TC2);
     else rc = launch_fwd_simt(a, L, ws, q, ori_kv, ori_block_table, cmp_kv, cmp_block_table, sinks, out, lse, s);
     if (rc) return rc;
     return record_kernel_event(false, s);

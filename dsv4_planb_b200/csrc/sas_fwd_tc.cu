@@ -214,15 +214,19 @@ __device__ __forceinline__ Item load_unit(const TcArgs &p, int u) {
     return it;
 }
 
+// What the helpers below need of a kernel's shared header: its abort flag and its unit queue
+// (both kernels lay these out in their own header struct).
 struct Sync {
-    Hdr *h;
+    volatile int *abort;
     uint32_t *status;
     uint32_t peer_abort;  // shared::cluster address of the peer CTA's abort flag
+    uint64_t *tq_full, *tq_empty;
+    volatile int *tq;
 };
 
 __device__ __noinline__ void raise_abort(const Sync &s, uint32_t bits) {
     sas::set_status(s.status, bits);
-    s.h->abort = 1;
+    *s.abort = 1;
     st_cluster_u32(s.peer_abort, 1u);
 }
 
@@ -232,7 +236,7 @@ __device__ __forceinline__ bool wait_bar(const Sync &s, uint32_t bar, uint32_t p
     for (uint32_t it = 0;; ++it) {
         if (cluster_scope ? mbar_try_cluster(bar, parity) : mbar_try(bar, parity)) return true;
         if ((it & 15u) == 15u) {
-            if (s.h->abort) return false;
+            if (*s.abort) return false;
             const uint64_t now = globaltimer();
             if (t0 == 0) t0 = now;
             else if (now - t0 > kTimeoutNs) {
@@ -278,11 +282,11 @@ __device__ __forceinline__ bool tq_read(const TcArgs &p, const Sync &sy, uint32_
         return true;
     }
     const int s = (k - 1) % kTq;
-    if (!wait_warp(sy, smem_u32(&sy.h->tq_full[s]), ((k - 1) / kTq) & 1, true)) return false;
-    t = sy.h->tq[s];
+    if (!wait_warp(sy, smem_u32(&sy.tq_full[s]), ((k - 1) / kTq) & 1, true)) return false;
+    t = sy.tq[s];
     __syncwarp();
     if ((threadIdx.x & 31) == 0) {
-        const uint32_t e = smem_u32(&sy.h->tq_empty[s]);
+        const uint32_t e = smem_u32(&sy.tq_empty[s]);
         if (rank == 0)
             mbar_arrive(e);
         else
@@ -301,17 +305,17 @@ __device__ __forceinline__ bool tq_publish(const TcArgs &p, const Sync &sy, uint
     }
     const int s = (k - 1) % kTq;
     const int lane = threadIdx.x & 31;
-    if (k - 1 >= (uint32_t)kTq && !wait_warp(sy, smem_u32(&sy.h->tq_empty[s]), (((k - 1) / kTq) - 1) & 1))
+    if (k - 1 >= (uint32_t)kTq && !wait_warp(sy, smem_u32(&sy.tq_empty[s]), (((k - 1) / kTq) - 1) & 1))
         return false;
     int v = 0;
     if (lane == 0) {
         if (pend < 0) pend = (int)ncluster_x() + atomicAdd(p.counter, 1);
         v = pend < p.U ? pend : -1;
         pend = -1;
-        sy.h->tq[s] = v;
-        st_cluster_u32(map_to_cta(smem_u32((const void *)&sy.h->tq[s]), 1), (uint32_t)v);
-        mbar_arrive(smem_u32(&sy.h->tq_full[s]));
-        mbar_arrive_remote(map_to_cta(smem_u32(&sy.h->tq_full[s]), 1));
+        sy.tq[s] = v;
+        st_cluster_u32(map_to_cta(smem_u32((const void *)&sy.tq[s]), 1), (uint32_t)v);
+        mbar_arrive(smem_u32(&sy.tq_full[s]));
+        mbar_arrive_remote(map_to_cta(smem_u32(&sy.tq_full[s]), 1));
     }
     t = __shfl_sync(0xffffffffu, v, 0);
     return true;
@@ -562,7 +566,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the combine kernel (split KV) may be scheduled now; it waits for this grid's completion
     if constexpr (kSplit) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const uint32_t tmem = hd->tmem_base;
-    Sync sy{hd, p.status, map_to_cta(smem_u32((const void *)&hd->abort), rank ^ 1u)};
+    Sync sy{&hd->abort, p.status, map_to_cta(smem_u32((const void *)&hd->abort), rank ^ 1u), hd->tq_full, hd->tq_empty,
+            hd->tq};
 
     if (rank == 0) {
         // ======================= score CTA =======================
@@ -979,6 +984,536 @@ done:
     if (warp == kMmaWarp) tmem_dealloc(tmem, kTmemCols);
 }
 
+// ============================================================================================
+// fwd_tc2_kernel: the same computation as fwd_tc_kernel, decomposed over a CTA pair with one
+// cta_group::2 MMA stream instead of split roles.
+//
+// A tile of 64 keys is split between the two SMs: CTA r gathers the full rows of tile keys
+// [32 r, 32 r + 32) (QK's B operand: a 2-SM MMA takes N/2 columns of B from each CTA) and the
+// value dims it supplies to PV of the other 32 keys (PV's B operand is split along N = value dims,
+// so each CTA needs its dims of all 64 keys).  Per SM and tile that is 32 x 1152 + 32 x 512 bytes
+// instead of the 64 x 1152 bytes the score CTA of fwd_tc_kernel gathers; the measured per-SM row
+// gather rate (~38 GB/s) bounds either kernel.
+//
+// CTA r holds heads [64 r, 64 r + 64): both MMAs are M = 128 over the pair, so each CTA receives
+// its 64 heads' S (64 keys) and O (512 value dims).  2-SM accumulator layout in each CTA's TMEM:
+// row m's first N/2 columns in lane m, its last N/2 in lane m + 64, N/2 columns wide.
+//
+//   TMEM (per CTA)  O: cols [0, 256)  (hf = 0, 1: value dims 256 hf + [0, 256), 128 cols each)
+//                   S: cols [256, 320) (two buffers of 32)
+//                   Q: cols [320, 512) (dims [0, 384) of the CTA's 64 heads, A operand: row m in
+//                      lanes m and m + 64)
+//   SMEM (per CTA)  Q dims [384, D_qk) (SS part of QK), K ring (3 x 32 rows x 9 slabs), PV operand
+//                   ring (2 x 64 keys x 4 slabs: this CTA's value dims), P ring (2 x 64 x 64 bf16)
+//
+//   warps 0-3  softmax of the CTA's 64 heads: thread i holds head i % 64 and keys (or O columns)
+//              of half i / 64; the two halves of a head exchange max and sums through shared memory.
+//              Also the unit's Q (registers -> TMEM / shared memory), the O rescale of its own lane,
+//              and the epilogue.
+//   warps 4-5  gather the CTA's own 32 key rows (all slabs) into the K ring
+//   warps 6-7  gather the other CTA's 32 keys' value slabs of this CTA into the PV operand ring
+//   warp 8     CTA 0: issues QK(j), then PV(j - 1), and the commits (multicast to both CTAs);
+//              both: TMEM allocation (cta_group::2 needs the same warp in both CTAs)
+//   warp 9     copies the own keys' value slabs from the K ring into the PV operand ring; in CTA 1
+//              it also tells CTA 0 when this CTA's K and PV stages are complete
+// ============================================================================================
+
+constexpr int kT2Threads = 320;
+constexpr int kT2KStages = 3, kT2VStages = 2, kT2PStages = 2;
+constexpr int kT2Half = 32;                                 // keys of a tile each CTA gathers in full
+constexpr int kT2Slab = kT2Half * 128;                      // one 64-dim slab of 32 rows
+constexpr int kT2KStage = 9 * kT2Slab;                      // 36 KiB
+constexpr int kT2VBlock = kBK * 128;                        // 64 keys x 64 dims
+constexpr int kT2VStage = 4 * kT2VBlock;                    // this CTA's 256 value dims, 32 KiB
+constexpr int kT2PStage = 64 * kBK * 2;                     // 64 heads x 64 keys bf16, 8 KiB
+constexpr int kT2QTmemDims = 384;                           // Q dims in TMEM (A operand)
+constexpr int kT2QSmem = (kMaxDq - kT2QTmemDims) / 64 * 64 * 128;  // dims [384, 576): 3 slabs of 64 rows
+constexpr int kT2TmemO = 0, kT2TmemS = 256, kT2TmemQ = 320;
+constexpr uint32_t kT2TqReaders = 18;  // CTA 0: warps 0-3, 5-9; CTA 1: warps 0-7, 9
+
+struct Hdr2 {
+    uint64_t k_full[kT2KStages], k_empty[kT2KStages], k_peer[kT2KStages];
+    uint64_t v_full[kT2VStages], v_empty[kT2VStages], v_peer[kT2VStages];
+    uint64_t s_full[2], s_free[2], p_ready[kT2PStages], p_free[kT2PStages];
+    uint64_t pv_done, o_full, o_empty, q_ready;
+    uint64_t tq_full[kTq], tq_empty[kTq];
+    volatile int tq[kTq];
+    uint32_t tmem_base;
+    volatile int abort;
+    alignas(16) int32_t krow[kT2KStages][kT2Half];  // own keys' rows of the tile in each K stage
+    alignas(16) int32_t vrow[kT2VStages][kT2Half];  // the other CTA's keys' rows, per PV stage
+    float xch[4][128];                               // pair exchange: max, sum, rounded sum
+};
+constexpr int kT2Hdr = 4096;
+static_assert(sizeof(Hdr2) <= kT2Hdr, "tc2 header");
+constexpr int kT2OffQ = kT2Hdr;
+constexpr int kT2OffK = kT2OffQ + kT2QSmem;
+constexpr int kT2OffV = kT2OffK + kT2KStages * kT2KStage;
+constexpr int kT2OffP = kT2OffV + kT2VStages * kT2VStage;
+constexpr int kT2Smem = kT2OffP + kT2PStages * kT2PStage + 1024;  // + alignment slack
+static_assert(kT2OffK % 1024 == 0 && kT2OffV % 1024 == 0 && kT2OffP % 1024 == 0, "tc2 smem alignment");
+static_assert(kT2Smem <= 232448, "tc2 smem");
+
+// Arrive on mbarrier `bar` of CTA 0 (a local arrive in CTA 0, a remote one from CTA 1).
+__device__ __forceinline__ void arrive_leader(uint32_t bar, uint32_t rank) {
+    if (rank == 0) mbar_arrive(bar);
+    else mbar_arrive_remote(map_to_cta(bar, 0));
+}
+
+// Rows of 32 keys of tile j (tile keys [k0, k0 + 32)) into `dst`, after the row lookups of the
+// previous call (fetched) and the next lookups issued (one tile ahead).  Thread kt < 32 of a
+// 64-thread group owns key k0 + kt.
+__device__ __forceinline__ void t2_rows(const TcArgs &p, const Item &it, const int32_t *crow, int j, int k0, int kt,
+                                        int32_t &fetched, int32_t *dst) {
+    if (kt < kT2Half) {
+        dst[kt] = key_row(p, it, j, k0 + kt, fetched);
+        fetched = j + 1 < it.j1 ? key_fetch(p, it, crow, j + 1, k0 + kt) : -1;
+    }
+}
+
+template <bool kBF16, bool kSplit>
+__global__ void __launch_bounds__(kT2Threads, 1)
+    fwd_tc2_kernel(const TcArgs p, const __grid_constant__ CUtensorMap ori_map,
+                   const __grid_constant__ CUtensorMap cmp_map) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    Hdr2 *hd = reinterpret_cast<Hdr2 *>(smem);
+    uint8_t *qs = smem + kT2OffQ, *kring = smem + kT2OffK, *vring = smem + kT2OffV, *pring = smem + kT2OffP;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const int nsl = p.Dq / 64;  // slabs of a key row
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kT2KStages; ++i) {
+            mbar_init(smem_u32(&hd->k_full[i]), 1);
+            mbar_init(smem_u32(&hd->k_empty[i]), 2);  // the MMAs' commit and this CTA's copy warp
+            mbar_init(smem_u32(&hd->k_peer[i]), 1);
+        }
+        for (int i = 0; i < kT2VStages; ++i) {
+            mbar_init(smem_u32(&hd->v_full[i]), 2);  // the gathering group and the copy warp
+            mbar_init(smem_u32(&hd->v_empty[i]), 1);
+            mbar_init(smem_u32(&hd->v_peer[i]), 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(smem_u32(&hd->s_full[i]), 1);
+            mbar_init(smem_u32(&hd->s_free[i]), 8);  // four softmax warps in each CTA
+        }
+        for (int i = 0; i < kT2PStages; ++i) {
+            mbar_init(smem_u32(&hd->p_ready[i]), 8);
+            mbar_init(smem_u32(&hd->p_free[i]), 1);
+        }
+        mbar_init(smem_u32(&hd->pv_done), 1);
+        mbar_init(smem_u32(&hd->o_full), 1);
+        mbar_init(smem_u32(&hd->o_empty), 8);
+        mbar_init(smem_u32(&hd->q_ready), 8);
+        for (int i = 0; i < kTq; ++i) {
+            mbar_init(smem_u32(&hd->tq_full[i]), 1);
+            mbar_init(smem_u32(&hd->tq_empty[i]), kT2TqReaders);
+        }
+        hd->abort = 0;
+        mbar_fence_init();
+    }
+    if (warp == 8) {
+        tmem_alloc2(smem_u32(&hd->tmem_base), kTmemCols);
+        tmem_relinquish2();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    tc_fence_after();
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if constexpr (kSplit) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const uint32_t tmem = hd->tmem_base;
+    Sync sy{&hd->abort, p.status, map_to_cta(smem_u32((const void *)&hd->abort), rank ^ 1u), hd->tq_full, hd->tq_empty,
+            hd->tq};
+
+    if (warp >= 4 && warp < 8) {
+        // ------------------------------ gathers ------------------------------
+        const bool own = warp < 6;               // warps 4-5: own rows; 6-7: the other CTA's keys' value slabs
+        const int gt = threadIdx.x - (own ? 128 : 192);
+        const bool writer = rank == 0 && warp == 4;
+        const int k0 = own ? kT2Half * (int)rank : kT2Half * (int)(rank ^ 1u);
+        const int bar_id = own ? 2 : 3;
+        uint32_t cnt = 0;
+        int pend = -1;
+        for (uint32_t k = 0;; ++k) {
+            int t = -1;
+            const bool got = writer ? tq_publish(p, sy, k, pend, t) : tq_read(p, sy, rank, k, t);
+            if (!bar_red_and(bar_id, 64, got)) break;
+            if (t < 0) break;
+            const Item it = load_unit<kSplit>(p, t);
+            if (it.skip) continue;
+            const int32_t *crow = p.rows + (int64_t)it.t * p.row_cap;
+            int32_t fetched = gt < kT2Half && it.j1 > it.j0 ? key_fetch(p, it, crow, it.j0, k0 + gt) : -1;
+            for (int j = it.j0; j < it.j1; ++j, ++cnt) {
+                const int stages = own ? kT2KStages : kT2VStages;
+                const int st = cnt % stages;
+                uint64_t *full = own ? &hd->k_full[st] : &hd->v_full[st];
+                uint64_t *empty = own ? &hd->k_empty[st] : &hd->v_empty[st];
+                int32_t *rows = own ? hd->krow[st] : hd->vrow[st];
+                const bool ok = wait_warp(sy, smem_u32(empty), ((cnt / stages) & 1) ^ 1, true);
+                if (ok) t2_rows(p, it, crow, j, k0, gt, fetched, rows);
+                const uint32_t bytes = own ? (uint32_t)nsl * kT2Slab : 4u * kT2Half * 128;
+                if (ok && gt == 0) mbar_arrive_expect_tx(smem_u32(full), bytes);
+                if (!bar_red_and(bar_id, 64, ok)) goto done;
+                if (writer && gt == 0 && j == (it.j1 - it.j0 > 1 ? it.j1 - 2 : it.j0))
+                    pend = (int)ncluster_x() + atomicAdd(p.counter, 1);
+                const bool win = j < it.nwt;
+                const int32_t oob = win ? p.ori_rows : p.cmp_rows;
+                const CUtensorMap *map = win ? &ori_map : &cmp_map;
+                if (own) {
+                    // slab s, quad q (rows 4q .. 4q + 3 of the CTA's 32 keys) -> K stage slab s
+                    const uint32_t base = smem_u32(kring + (size_t)st * kT2KStage);
+                    for (int g = gt; g < nsl * 8; g += 64) {
+                        const int s = g >> 3, q = g & 7;
+                        const int4 r4 = reinterpret_cast<const int4 *>(rows)[q];
+                        tma_gather4(base + s * kT2Slab + q * 512, map, s * 64, r4.x >= 0 ? r4.x : oob,
+                                    r4.y >= 0 ? r4.y : oob, r4.z >= 0 ? r4.z : oob, r4.w >= 0 ? r4.w : oob,
+                                    smem_u32(full));
+                    }
+                } else if (gt < 32) {
+                    // block b = (hf, s) of this CTA's value dims (global slab 4 hf + 2 rank + s), quad q of
+                    // the other CTA's keys -> PV stage rows k0 + 4q ..
+                    const int b = gt >> 3, q = gt & 7, gs = 4 * (b >> 1) + 2 * (int)rank + (b & 1);
+                    const uint32_t base = smem_u32(vring + (size_t)st * kT2VStage);
+                    const int4 r4 = reinterpret_cast<const int4 *>(rows)[q];
+                    tma_gather4(base + b * kT2VBlock + (k0 + 4 * q) * 128, map, gs * 64, r4.x >= 0 ? r4.x : oob,
+                                r4.y >= 0 ? r4.y : oob, r4.z >= 0 ? r4.z : oob, r4.w >= 0 ? r4.w : oob,
+                                smem_u32(full));
+                }
+            }
+        }
+    } else if (warp == 9) {
+        // --------------- own value slabs -> PV stage; CTA 1 reports its stages to CTA 0 ---------------
+        uint32_t kc = 0, vc = 0;
+        for (uint32_t k = 0;; ++k) {
+            int t;
+            if (!tq_read(p, sy, rank, k, t)) goto done;
+            if (t < 0) break;
+            const Item it = load_unit<kSplit>(p, t);
+            if (it.skip) continue;
+            for (int j = it.j0; j < it.j1; ++j, ++kc, ++vc) {
+                const int ks = kc % kT2KStages, vs = vc % kT2VStages;
+                if (!wait_warp(sy, smem_u32(&hd->k_full[ks]), (kc / kT2KStages) & 1)) goto done;
+                if (rank == 1 && lane == 0) mbar_arrive_remote(map_to_cta(smem_u32(&hd->k_peer[ks]), 0));
+                if (!wait_warp(sy, smem_u32(&hd->v_empty[vs]), ((vc / kT2VStages) & 1) ^ 1, true)) goto done;
+                // four 4 KiB blocks (32 rows x 128 B each, the same swizzle phase at both places)
+                const uint8_t *ksrc = kring + (size_t)ks * kT2KStage;
+                uint8_t *vdst = vring + (size_t)vs * kT2VStage + kT2Half * (int)rank * 128;
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    const int gs = 4 * (b >> 1) + 2 * (int)rank + (b & 1);
+                    const uint4 *src = reinterpret_cast<const uint4 *>(ksrc + gs * kT2Slab);
+                    uint4 *dst = reinterpret_cast<uint4 *>(vdst + b * kT2VBlock);
+#pragma unroll
+                    for (int e = 0; e < kT2Slab / 16 / 32; ++e) dst[lane + 32 * e] = src[lane + 32 * e];
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(smem_u32(&hd->v_full[vs]));
+                    mbar_arrive(smem_u32(&hd->k_empty[ks]));
+                }
+                if (rank == 1) {
+                    if (!wait_warp(sy, smem_u32(&hd->v_full[vs]), (vc / kT2VStages) & 1)) goto done;
+                    if (lane == 0) mbar_arrive_remote(map_to_cta(smem_u32(&hd->v_peer[vs]), 0));
+                }
+            }
+        }
+    } else if (warp == 8) {
+        // ------------------------------ MMA (CTA 0) ------------------------------
+        if (rank != 0) goto done;
+        const uint32_t idesc_s = idesc_f16(kBF16 ? 1u : 0u, 128, kBK, 0);
+        const uint32_t idesc_o = idesc_f16(kBF16 ? 1u : 0u, 128, 256, 1);
+        const int nk = p.Dq / 16, nk_t = kT2QTmemDims / 16;
+        uint32_t kc = 0, sc = 0, vc = 0, qc = 0, oc = 0;
+        for (uint32_t k = 0;; ++k) {
+            int t;
+            if (!tq_read(p, sy, rank, k, t)) goto done;
+            if (t < 0) break;
+            const Item it = load_unit<kSplit>(p, t);
+            if (it.skip || it.ntiles == 0) continue;
+            if (!wait_warp(sy, smem_u32(&hd->q_ready), qc & 1, true)) goto done;
+            ++qc;
+            for (int j = it.j0; j <= it.j1; ++j) {
+                if (j < it.j1) {
+                    // QK(j)
+                    const int ks = kc % kT2KStages, sb = sc & 1;
+                    if (!wait_warp(sy, smem_u32(&hd->k_full[ks]), (kc / kT2KStages) & 1)) goto done;
+                    if (!wait_warp(sy, smem_u32(&hd->k_peer[ks]), (kc / kT2KStages) & 1, true)) goto done;
+                    if (!wait_warp(sy, smem_u32(&hd->s_free[sb]), ((sc >> 1) & 1) ^ 1, true)) goto done;
+                    tc_fence_after();
+                    if (lane == 0) {
+                        const uint32_t kb = smem_u32(kring + (size_t)ks * kT2KStage);
+                        const uint32_t d = tmem + kT2TmemS + sb * kT2Half;
+                        for (int kk = 0; kk < nk; ++kk) {
+                            const uint64_t bdesc = sdesc_sw128(kb + (kk >> 2) * kT2Slab + (kk & 3) * 32, 16, 1024);
+                            if (kk < nk_t) {
+                                mma2_ts(d, tmem + kT2TmemQ + kk * 8, bdesc, idesc_s, kk > 0 ? 1u : 0u);
+                            } else {
+                                const uint64_t adesc =
+                                    sdesc_sw128(smem_u32(qs) + ((kk - nk_t) >> 2) * (64 * 128) + (kk & 3) * 32, 16, 1024);
+                                mma2_ss(d, adesc, bdesc, idesc_s, 1u);
+                            }
+                        }
+                        tc2_commit_mc(smem_u32(&hd->s_full[sb]), 3);
+                        tc2_commit_mc(smem_u32(&hd->k_empty[ks]), 3);
+                    }
+                    __syncwarp();
+                    ++kc;
+                    ++sc;
+                }
+                if (j > it.j0) {
+                    // PV(j - 1)
+                    const int vs = vc % kT2VStages, ps = vc % kT2PStages;
+                    const bool first = j - 1 == it.j0, last = j - 1 == it.j1 - 1;
+                    if (first && !wait_warp(sy, smem_u32(&hd->o_empty), (oc & 1) ^ 1, true)) goto done;
+                    if (!wait_warp(sy, smem_u32(&hd->p_ready[ps]), (vc / kT2PStages) & 1, true)) goto done;
+                    if (!wait_warp(sy, smem_u32(&hd->v_full[vs]), (vc / kT2VStages) & 1)) goto done;
+                    if (!wait_warp(sy, smem_u32(&hd->v_peer[vs]), (vc / kT2VStages) & 1, true)) goto done;
+                    tc_fence_after();
+                    if (lane == 0) {
+                        const bool stall = p.test_stall && vc == 0;  // test hook, see SAS_FWD_FLAG_TEST_STALL
+                        const uint32_t pa = smem_u32(pring + (size_t)ps * kT2PStage);
+                        const uint32_t vb = smem_u32(vring + (size_t)vs * kT2VStage);
+                        for (int hf = 0; hf < 2; ++hf)
+                            for (int kk = 0; kk < kBK / 16; ++kk)
+                                mma2_ss(tmem + kT2TmemO + hf * 128, sdesc_sw128(pa + kk * 32, 16, 1024),
+                                        sdesc_sw128(vb + hf * 2 * kT2VBlock + kk * 2048, kT2VBlock, 1024), idesc_o,
+                                        (!first || kk > 0) ? 1u : 0u);
+                        if (!stall) tc2_commit_mc(smem_u32(&hd->p_free[ps]), 3);
+                        tc2_commit_mc(smem_u32(&hd->v_empty[vs]), 3);
+                        tc2_commit_mc(smem_u32(&hd->pv_done), 3);
+                        if (last) tc2_commit_mc(smem_u32(&hd->o_full), 3);
+                    }
+                    __syncwarp();
+                    ++vc;
+                    if (last) ++oc;
+                }
+            }
+        }
+    } else {
+        // ------------------------------ softmax, Q, epilogue (warps 0-3) ------------------------------
+        const int i = threadIdx.x, half = i >> 6, r = i & 63;
+        const int head = 64 * (int)rank + r;
+        const bool hv = head < p.N1;
+        const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+        const float sink2 = hv ? p.sinks[head] * 1.4426950408889634f : 0.f;
+        typedef typename std::conditional<kBF16, __nv_bfloat16, __half>::type OT;
+        uint32_t sc = 0, oc = 0;
+        for (uint32_t k = 0;; ++k) {
+            int t;
+            if (!tq_read(p, sy, rank, k, t)) goto done;
+            if (t < 0) break;
+            const Item it = load_unit<kSplit>(p, t);
+            if (it.skip) continue;
+            t = it.t;
+            if (it.ntiles == 0) {
+                if (hv) {
+                    OT *orow = reinterpret_cast<OT *>(p.out) + ((int64_t)t * p.N1 + head) * p.Dv;
+                    for (int hf = 0; hf < 2; ++hf)
+                        for (int d = 0; d < 128; d += 8)
+                            *reinterpret_cast<uint4 *>(orow + 256 * hf + 128 * half + d) = make_uint4(0, 0, 0, 0);
+                    if (half == 0 && p.lse) p.lse[(int64_t)t * p.N1 + head] = it.valid ? p.sinks[head] : 0.f;
+                }
+                continue;
+            }
+            // ---- Q of the unit: dims [0, 384) -> TMEM (both lanes of the head), [384, D_qk) -> smem
+            // (each half writes half of the row).  The previous unit's QK products are complete: this
+            // warp waited for their S.
+            {
+                const uint4 *qrow = reinterpret_cast<const uint4 *>(
+                    reinterpret_cast<const uint16_t *>(p.q) + ((int64_t)t * p.N1 + (hv ? head : 0)) * p.Dq);
+                for (int c = 0; c < kT2QTmemDims / 64; ++c) {
+                    uint32_t w[32];
+#pragma unroll
+                    for (int v = 0; v < 8; ++v) {
+                        const uint4 x = hv ? __ldg(qrow + c * 8 + v) : make_uint4(0, 0, 0, 0);
+                        w[4 * v] = x.x;
+                        w[4 * v + 1] = x.y;
+                        w[4 * v + 2] = x.z;
+                        w[4 * v + 3] = x.w;
+                    }
+                    tmem_st32(tmem + lane_base + kT2TmemQ + c * 32, w);
+                }
+                const int nq = (p.Dq - kT2QTmemDims) / 8;  // 16-byte chunks of the smem part
+                for (int c = half * (nq / 2); c < (half + 1) * (nq / 2); ++c) {
+                    const int s = c >> 3, cc = c & 7;
+                    const uint4 x = hv ? __ldg(qrow + kT2QTmemDims / 8 + c) : make_uint4(0, 0, 0, 0);
+                    *reinterpret_cast<uint4 *>(qs + s * (64 * 128) + (r >> 3) * 1024 + (r & 7) * 128 +
+                                               ((cc ^ (r & 7)) << 4)) = x;
+                }
+                tc_wait_st();
+                fence_proxy_async_smem();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) arrive_leader(smem_u32(&hd->q_ready), rank);
+            }
+            float m = it.piece == 0 ? sink2 : -INFINITY, l = it.piece == 0 ? 1.f : 0.f, lr = l;
+            for (int j = it.j0; j < it.j1; ++j, ++sc) {
+                const int sb = sc & 1, ps = sc % kT2PStages;
+                if (!wait_warp(sy, smem_u32(&hd->s_full[sb]), (sc >> 1) & 1, true)) goto done;
+                tc_fence_after();
+                uint32_t sr[32];
+                tmem_ld32(tmem + lane_base + kT2TmemS + sb * kT2Half, sr);
+                tc_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) arrive_leader(smem_u32(&hd->s_free[sb]), rank);
+                const int nvalid = j < it.nwt ? min(kBK, it.n_win - j * kBK) : min(kBK, it.n_cmp - (j - it.nwt) * kBK);
+                const int kv = nvalid - kT2Half * half;  // valid keys among this half's 32
+                float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+                for (int c = 0; c < kT2Half; ++c) {
+                    const float x = c < kv ? __uint_as_float(sr[c]) * p.scale_log2 : -INFINITY;
+                    sr[c] = __float_as_uint(x);
+                    mx4[c & 3] = fmaxf(mx4[c & 3], x);
+                }
+                hd->xch[0][i] = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                const float mx = fmaxf(hd->xch[0][i], hd->xch[0][i ^ 64]);
+                float alpha = 1.f;
+                if (j == it.j0) {
+                    const float mn = fmaxf(m, mx);
+                    const float a0 = exp2f(m - mn);
+                    l *= a0;
+                    lr *= a0;
+                    m = mn;
+                } else if (mx > m + p.tau) {
+                    alpha = exp2f(m - mx);
+                    l *= alpha;
+                    lr *= alpha;
+                    m = mx;
+                }
+                uint32_t pk[16];
+                float sum4[4] = {0.f, 0.f, 0.f, 0.f}, sumr4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int c = 0; c < kT2Half; c += 2) {
+                    const float p0 = ex2_approx(__uint_as_float(sr[c]) - m);
+                    const float p1 = ex2_approx(__uint_as_float(sr[c + 1]) - m);
+                    float &sum = sum4[(c >> 1) & 3], &sumr = sumr4[(c >> 1) & 3];
+                    sum += p0 + p1;
+                    float2 pr;
+                    if constexpr (kBF16) {
+                        __nv_bfloat162 v = __floats2bfloat162_rn(p0, p1);
+                        pk[c >> 1] = *reinterpret_cast<uint32_t *>(&v);
+                        pr = __bfloat1622float2(v);
+                    } else {
+                        __half2 v = __floats2half2_rn(p0, p1);
+                        pk[c >> 1] = *reinterpret_cast<uint32_t *>(&v);
+                        pr = __half22float2(v);
+                    }
+                    sumr += pr.x + pr.y;
+                }
+                hd->xch[1][i] = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
+                hd->xch[2][i] = (sumr4[0] + sumr4[1]) + (sumr4[2] + sumr4[3]);
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                // the two halves add their partial sums in the same order, so both keep identical state
+                const int i0 = i & 63, i1 = i0 + 64;
+                l += hd->xch[1][i0] + hd->xch[1][i1];
+                lr += hd->xch[2][i0] + hd->xch[2][i1];
+                // P of this half's 32 keys -> chunks 4 half .. 4 half + 3 of row r (SW128 K-major)
+                if (!wait_warp(sy, smem_u32(&hd->p_free[ps]), ((sc / kT2PStages) & 1) ^ 1, true)) goto done;
+                uint8_t *prow = pring + (size_t)ps * kT2PStage + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int cc = 4 * half + q;
+                    *reinterpret_cast<uint4 *>(prow + ((cc ^ (r & 7)) << 4)) =
+                        make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+                }
+                fence_proxy_async_smem();
+                if (__any_sync(0xffffffffu, alpha != 1.f) && j > it.j0) {
+                    // rescale this lane's O: every PV product so far (the last one is tile j - 1's) has completed
+                    if (!wait_warp(sy, smem_u32(&hd->pv_done), (sc - 1) & 1, true)) goto done;
+                    tc_fence_after();
+#pragma unroll
+                    for (int c = 0; c < 256 / 32; c += 4) {
+                        uint32_t r0[32], r1[32], r2[32], r3[32];
+                        tmem_ld32(tmem + lane_base + kT2TmemO + c * 32, r0);
+                        tmem_ld32(tmem + lane_base + kT2TmemO + (c + 1) * 32, r1);
+                        tmem_ld32(tmem + lane_base + kT2TmemO + (c + 2) * 32, r2);
+                        tmem_ld32(tmem + lane_base + kT2TmemO + (c + 3) * 32, r3);
+                        tc_wait_ld();
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) {
+                            r0[e] = __float_as_uint(__uint_as_float(r0[e]) * alpha);
+                            r1[e] = __float_as_uint(__uint_as_float(r1[e]) * alpha);
+                            r2[e] = __float_as_uint(__uint_as_float(r2[e]) * alpha);
+                            r3[e] = __float_as_uint(__uint_as_float(r3[e]) * alpha);
+                        }
+                        tmem_st32(tmem + lane_base + kT2TmemO + c * 32, r0);
+                        tmem_st32(tmem + lane_base + kT2TmemO + (c + 1) * 32, r1);
+                        tmem_st32(tmem + lane_base + kT2TmemO + (c + 2) * 32, r2);
+                        tmem_st32(tmem + lane_base + kT2TmemO + (c + 3) * 32, r3);
+                    }
+                    tc_wait_st();
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) arrive_leader(smem_u32(&hd->p_ready[ps]), rank);
+            }
+            // ---- epilogue: O of this lane (value dims 256 hf + 128 half + [0, 128)) / lr
+            if (!wait_warp(sy, smem_u32(&hd->o_full), oc & 1, true)) goto done;
+            ++oc;
+            tc_fence_after();
+            const float inv = 1.f / lr;
+            if (it.np == 1) {
+                OT *orow = reinterpret_cast<OT *>(p.out) + ((int64_t)t * p.N1 + (hv ? head : 0)) * p.Dv;
+                for (int hf = 0; hf < 2; ++hf)
+                    for (int c = 0; c < 4; ++c) {
+                        uint32_t w[32];
+                        tmem_ld32(tmem + lane_base + kT2TmemO + hf * 128 + c * 32, w);
+                        tc_wait_ld();
+                        if (hv) {
+                            float x[32];
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) x[e] = __uint_as_float(w[e]) * inv;
+                            store_row32<kBF16>(orow + 256 * hf + 128 * half + 32 * c, x);
+                        }
+                    }
+                if (hv && half == 0 && p.lse) p.lse[(int64_t)t * p.N1 + head] = (m + log2f(l)) * 0.6931471805599453f;
+            } else if constexpr (kSplit) {
+                const int64_t sl = (int64_t)t * p.P + it.piece;
+                uint16_t *po = p.part_o + (sl * p.N1 + (hv ? head : 0)) * p.Dv;
+                for (int hf = 0; hf < 2; ++hf)
+                    for (int c = 0; c < 4; ++c) {
+                        uint32_t w[32];
+                        tmem_ld32(tmem + lane_base + kT2TmemO + hf * 128 + c * 32, w);
+                        tc_wait_ld();
+                        if (hv) {
+                            float x[32];
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) x[e] = __uint_as_float(w[e]) * inv;
+                            store_row32<true>(reinterpret_cast<__nv_bfloat16 *>(po + 256 * hf + 128 * half + 32 * c), x);
+                        }
+                    }
+                if (hv && half == 0) {
+                    float *pst = p.part_s + (sl * p.N1 + head) * 4;
+                    pst[0] = m;
+                    pst[1] = l;
+                    pst[2] = lr;
+                    pst[3] = 0.f;
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) arrive_leader(smem_u32(&hd->o_empty), rank);
+        }
+    }
+done:
+    __syncwarp();
+    if (hd->abort) {
+        const uint64_t t0 = globaltimer();
+        while (globaltimer() - t0 < 20000000ull) {
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    tc_fence_after();
+    if (warp == 8) tmem_dealloc2(tmem, kTmemCols);
+}
+
 // Merge of the pieces of split tokens (flash-decoding's LSE combine).  Block (t, h), thread =
 // 8 consecutive output columns.  With Mx = max m_i and w_i = lr_i 2^(m_i - Mx) over the token's
 // pieces in piece order: out = sum_i w_i o_i / sum_i w_i, lse = ln 2 (Mx + log2 sum_i l_i 2^(m_i - Mx)).
@@ -1228,9 +1763,10 @@ size_t tc_workspace(const SasFwdArgs &a) {
     return part_o_bytes(a, sp) + (size_t)a.num_tokens * sp.P * a.num_heads * 4 * sizeof(float);
 }
 
+// pair: the cta_group::2 kernel (fwd_tc2_kernel) instead of the role-split one (fwd_tc_kernel).
 int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const void *q, const void *ori_kv,
                   const int32_t *ori_bt, const void *cmp_kv, const int32_t *cmp_bt, const float *sinks, void *out,
-                  float *lse, cudaStream_t s) {
+                  float *lse, cudaStream_t s, bool pair) {
     if (a.num_tokens == 0) return SAS_OK;
     const bool bf16 = a.dtype == SAS_DTYPE_BF16;
     TcArgs p;
@@ -1277,10 +1813,13 @@ int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const 
     CUtensorMap q_map;  // q as [T * N1 rows][D_qk], boxes of 64 dims x 64 head rows
     rc = make_map(&q_map, q, (int64_t)a.num_tokens * a.num_heads, a.head_dim, bf16, 64);
     if (rc) return rc;
-    // four instantiations: element type x split
+    // four instantiations of each kernel: element type x split
     using KernelFn = void (*)(const TcArgs, const CUtensorMap, const CUtensorMap, const CUtensorMap);
     static const KernelFn kernels[4] = {fwd_tc_kernel<true, false>, fwd_tc_kernel<true, true>,
                                         fwd_tc_kernel<false, false>, fwd_tc_kernel<false, true>};
+    using Kernel2Fn = void (*)(const TcArgs, const CUtensorMap, const CUtensorMap);
+    static const Kernel2Fn kernels2[4] = {fwd_tc2_kernel<true, false>, fwd_tc2_kernel<true, true>,
+                                          fwd_tc2_kernel<false, false>, fwd_tc2_kernel<false, true>};
     // function attributes belong to a device's context: raised once per device and instantiation
     // (the first call on a device must come before any stream capture)
     int dev = 0;
@@ -1289,8 +1828,9 @@ int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const 
     static sas::DeviceOnce attr_done[sas::kMaxDevices];
     static std::atomic<int> num_sms[sas::kMaxDevices] = {};
     const int di = (bf16 ? 0 : 2) + (p.P > 1 ? 1 : 0);
-    int rc_attr = attr_done[dev].run(1u << di, [&] {
-        return check_cuda(cudaFuncSetAttribute(kernels[di], cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+    int rc_attr = attr_done[dev].run(1u << (di + (pair ? 4 : 0)), [&] {
+        return pair ? check_cuda(cudaFuncSetAttribute(kernels2[di], cudaFuncAttributeMaxDynamicSharedMemorySize, kT2Smem))
+                    : check_cuda(cudaFuncSetAttribute(kernels[di], cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
     });
     if (rc_attr) return rc_attr;
     int sms = num_sms[dev].load(std::memory_order_relaxed);
@@ -1301,8 +1841,8 @@ int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const 
     const int clusters = std::max(1, std::min(p.U, sms / 2));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * clusters, 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.blockDim = dim3(pair ? kT2Threads : kThreads, 1, 1);
+    cfg.dynamicSmemBytes = pair ? kT2Smem : kSmemBytes;
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1313,7 +1853,8 @@ int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const 
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kernels[di], p, ori_map, cmp_map, q_map);
+    cudaError_t e = pair ? cudaLaunchKernelEx(&cfg, kernels2[di], p, ori_map, cmp_map)
+                         : cudaLaunchKernelEx(&cfg, kernels[di], p, ori_map, cmp_map, q_map);
     if (check_cuda(e)) return SAS_ERR_CUDA;
     if (p.P > 1) {
         cudaLaunchConfig_t cc = {};

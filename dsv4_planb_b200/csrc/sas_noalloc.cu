@@ -25,7 +25,7 @@ int launch_fwd_simt(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, cons
 bool tc_supported(const SasFwdArgs &a);
 int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const void *q, const void *ori_kv,
                   const int32_t *ori_bt, const void *cmp_kv, const int32_t *cmp_bt, const float *sinks, void *out,
-                  float *lse, cudaStream_t s);
+                  float *lse, cudaStream_t s, bool pair);
 } // namespace sas_host
 
 namespace {
@@ -115,7 +115,8 @@ extern "C" int sas_forward_noalloc(const SasFwdArgs *args, const void *q, const 
     rc = sas_host::launch_prep(a, L, ws, cmp_block_table, cmp_indices, q_prefix, act_q_len, act_kv_len, s);
     if (rc) return rc;
     if (a.kernel != SAS_KERNEL_SIMT && sas_host::tc_supported(a))
-        return sas_host::launch_fwd_tc(a, L, ws, q, ori_kv, ori_block_table, cmp_kv, cmp_block_table, sinks, out, lse, s);
+        return sas_host::launch_fwd_tc(a, L, ws, q, ori_kv, ori_block_table, cmp_kv, cmp_block_table, sinks, out, lse, s,
+                                     a.kernel == SAS_KERNEL_TC2);
     return sas_host::launch_fwd_simt(a, L, ws, q, ori_kv, ori_block_table, cmp_kv, cmp_block_table, sinks, out, lse, s);
 }
 

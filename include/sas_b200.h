@@ -43,8 +43,15 @@ enum {
 
 typedef enum { SAS_DTYPE_BF16 = 0, SAS_DTYPE_FP16 = 1 } SasDtype;
 
-/* Kernel choice for sas_forward (SasFwdArgs.kernel). */
-typedef enum { SAS_KERNEL_AUTO = 0, SAS_KERNEL_SIMT = 1, SAS_KERNEL_TC = 2 } SasKernel;
+/*
+ * Kernel choice for sas_forward (SasFwdArgs.kernel).  SAS_KERNEL_TC: tensor
+ * cores, a two-SM cluster per unit that splits the work by role (one SM
+ * gathers K and computes S and P, the other gathers V and accumulates O).
+ * SAS_KERNEL_TC2: tensor cores, a two-SM cluster that issues one
+ * cta_group::2 MMA stream, each SM gathering half of every tile's key rows.
+ * Both take the same shapes (D_qk 512 or 576, D_v 512, up to 128 heads).
+ */
+typedef enum { SAS_KERNEL_AUTO = 0, SAS_KERNEL_SIMT = 1, SAS_KERNEL_TC = 2, SAS_KERNEL_TC2 = 3 } SasKernel;
 
 /*
  * Shape and mode of one sas_forward call.  Mirrors the compile-time

@@ -30,7 +30,7 @@ def _eager(wl, kernel):
     return out, lse
 
 
-@pytest.mark.parametrize("kernel,scenario", [("tc", 3), ("simt", 3), ("tc", 2), ("simt", 2)])
+@pytest.mark.parametrize("kernel,scenario", [("tc", 3), ("simt", 3), ("tc", 2), ("simt", 2), ("tc2", 3), ("tc2", 2)])
 def test_graph_capture_replays_new_inputs(cuda_device, kernel, scenario):
     """Scenario 3 (SCFA) and scenario 2 (CFA, whose dense compressed range the kernels take from
     the block table on the device: no host read of seqused_kv)."""

@@ -18,7 +18,7 @@ pytestmark = pytest.mark.gpu
 
 OUT_ATOL, OUT_RTOL = 2e-2, 1e-2
 LSE_ATOL = 1e-3
-KERNELS = ["simt", "tc"]
+KERNELS = ["simt", "tc", "tc2"]
 
 
 @pytest.fixture(scope="module")
@@ -64,11 +64,11 @@ def assert_close_to_golden(out, lse, exp_out, exp_lse, what):
 @pytest.mark.parametrize("kernel", KERNELS)
 @pytest.mark.parametrize("fixture_name", F.baseline_names())
 def test_baselines_match_reference_golden(api, cuda_device, kernel, fixture_name):
-    if kernel == "tc" and not tc_available():
+    if kernel.startswith("tc") and not tc_available():
         pytest.skip("tensor-core path not built for these shapes")
     case = F.load_case(fixture_name)
     wl = F.rebuild_baseline(case)
-    if kernel == "tc" and wl.q.shape[2] % 64:
+    if kernel.startswith("tc") and wl.q.shape[2] % 64:
         pytest.skip("tensor-core path needs D_qk % 64 == 0")
     out, lse = run(api, wl, kernel, cuda_device)
     toks = case["tokens"]
@@ -85,7 +85,7 @@ def test_baselines_match_reference_golden(api, cuda_device, kernel, fixture_name
 @pytest.mark.parametrize("kernel", KERNELS)
 @pytest.mark.parametrize("fixture_name", F.paramset_names())
 def test_reference_paramsets(api, cuda_device, kernel, fixture_name):
-    if kernel == "tc" and not tc_available():
+    if kernel.startswith("tc") and not tc_available():
         pytest.skip("tensor-core path not built for these shapes")
     name = fixture_name[len("paramset_"):-5]
     tag = fixture_name[-4:]
@@ -119,7 +119,7 @@ def test_reference_paramsets(api, cuda_device, kernel, fixture_name):
     # tolerance (mean |out - fp32 golden| 0.0066, CUDA-core kernel 0.0005); the
     # north-star bars against the fp32 golden (below) still hold.  bf16 inputs,
     # whose 8-bit mantissas give 16-bit products, pass at >= 99.73%.
-    fp16_tc = kernel == "tc" and tag == "fp16"
+    fp16_tc = kernel.startswith("tc") and tag == "fp16"
     ref_low = F.low_bits_to_f32(case["out_low_bits"], tag)
     pct, max_rel = F.check_result(out[toks], ref_low, tag)
     lpct, lmax_rel = F.check_lse(lse[toks], case["lse_low"], tag)
@@ -137,7 +137,7 @@ def test_reference_paramsets(api, cuda_device, kernel, fixture_name):
 
 @pytest.mark.parametrize("kernel", KERNELS)
 def test_bsnd_layout_and_return_types(api, cuda_device, kernel):
-    if kernel == "tc" and not tc_available():
+    if kernel.startswith("tc") and not tc_available():
         pytest.skip("tensor-core path not built")
     from dsv4_planb_b200 import workloads as W
 
@@ -209,7 +209,7 @@ def test_bad_index_and_block_flags(api, cuda_device):
 @pytest.mark.parametrize("kernel", KERNELS)
 def test_unmapped_blocks_read_as_zero_rows(api, cuda_device, kernel):
     """-1 table entries inside the used range behave like unpack_paged_kv's zero rows."""
-    if kernel == "tc" and not tc_available():
+    if kernel.startswith("tc") and not tc_available():
         pytest.skip("tensor-core path not built")
     from dsv4_planb_b200 import workloads as W
 
@@ -226,7 +226,7 @@ def test_unmapped_blocks_read_as_zero_rows(api, cuda_device, kernel):
 
 
 FULL_CONFIGS = [("c2", "tc"), ("c2", "simt"), ("c2", "tc-lazy"), ("c3", "tc"), ("c4", "tc"), ("c5", "tc"),
-                ("c4", "tc-lazy")]
+                ("c4", "tc-lazy"), ("c2", "tc2"), ("c2", "tc2-lazy"), ("c3", "tc2"), ("c4", "tc2"), ("c5", "tc2")]
 
 
 @pytest.mark.parametrize("cfg,kernel", FULL_CONFIGS, ids=[f"{c}-{k}" for c, k in FULL_CONFIGS])
@@ -238,10 +238,10 @@ def test_full_config_parity(api, cuda_device, cfg, kernel):
     middle and end of every request; 64 c5 requests spread over the length order) against the fp32
     oracle at the north-star bars, and size-independent properties on every token: finite, LSE at
     least the sink (the sink is one of the softmax's terms), |out| within max |V| (rows are convex
-    combinations of V rows).  "tc-lazy" is the tensor-core kernel with SAS_FWD_FLAG_LAZY_RESCALE."""
-    lazy = kernel == "tc-lazy"
-    kernel = "tc" if lazy else kernel
-    if kernel == "tc" and not tc_available():
+    combinations of V rows).  "-lazy" runs a tensor-core kernel with SAS_FWD_FLAG_LAZY_RESCALE."""
+    lazy = kernel.endswith("-lazy")
+    kernel = kernel[: -len("-lazy")] if lazy else kernel
+    if kernel.startswith("tc") and not tc_available():
         pytest.skip("tensor-core path not built")
     from dsv4_planb_b200 import workloads as W
     from tests import _sampled as SM
@@ -273,8 +273,9 @@ def test_full_config_parity(api, cuda_device, cfg, kernel):
     assert_close_to_golden(out, lse, ref_out, ref_lse, f"{cfg} {kernel}")
 
 
+@pytest.mark.parametrize("kernel", ["tc", "tc2"])
 @pytest.mark.parametrize("batch", [1, 4, 16, 37])
-def test_split_kv_small_batches(api, cuda_device, batch):
+def test_split_kv_small_batches(api, cuda_device, batch, kernel):
     """Decode batches with at most half as many tokens as the tensor-core launch has clusters
     are cut into pieces (split KV) and merged by LSE in a second kernel.  The merged output
     must meet the golden bars, and repeated calls must give identical bits (the merge runs
@@ -284,8 +285,8 @@ def test_split_kv_small_batches(api, cuda_device, batch):
     from dsv4_planb_b200 import workloads as W
 
     wl = W.config_workload("c2", device=cuda_device, batch=batch)
-    out, lse = run(api, wl, "tc", cuda_device)
-    out2, lse2 = run(api, wl, "tc", cuda_device)
+    out, lse = run(api, wl, kernel, cuda_device)
+    out2, lse2 = run(api, wl, kernel, cuda_device)
     assert np.array_equal(out, out2) and np.array_equal(lse, lse2)
     sample = sorted({0, batch // 2, batch - 1})
     wl_c = wl.to("cpu")
@@ -298,7 +299,8 @@ def test_split_kv_small_batches(api, cuda_device, batch):
     assert_close_to_golden(out[sample], lse[sample], ref_out[sample], ref_lse[sample], f"split batch {batch}")
 
 
-def test_split_tiles_hint_on_a_request_shard(api, cuda_device):
+@pytest.mark.parametrize("kernel", ["tc", "tc2"])
+def test_split_tiles_hint_on_a_request_shard(api, cuda_device, kernel):
     """A c5-style request shard (a few long and many short requests) with the sharding layer's
     piece size: long tokens are cut across clusters and merged; parity on sampled tokens and
     identical bits on a second call."""
@@ -313,8 +315,8 @@ def test_split_tiles_hint_on_a_request_shard(api, cuda_device):
                          num_heads=n1, topk=topk, seed=7, device=cuda_device)
     split = S.split_hint(S.token_tiles(wl.q_lens, wl.kv_lens, topk))
     assert split > 0
-    out, lse = run(api, wl, "tc", cuda_device, split_tiles=split)
-    out2, lse2 = run(api, wl, "tc", cuda_device, split_tiles=split)
+    out, lse = run(api, wl, kernel, cuda_device, split_tiles=split)
+    out2, lse2 = run(api, wl, kernel, cuda_device, split_tiles=split)
     assert np.array_equal(out, out2) and np.array_equal(lse, lse2)
     sample = [0, 1, 40, 95]
     wl_c = wl.to("cpu")
@@ -327,9 +329,10 @@ def test_split_tiles_hint_on_a_request_shard(api, cuda_device):
     assert_close_to_golden(out[sample], lse[sample], ref_out[sample], ref_lse[sample], f"shard split {split}")
 
 
+@pytest.mark.parametrize("kernel", ["tc", "tc2"])
 @pytest.mark.parametrize("dtype,heads,split", [(torch.float16, 128, 0), (torch.bfloat16, 64, 0),
                                                (torch.float16, 64, 6)])
-def test_split_kv_dtypes_and_heads(api, cuda_device, dtype, heads, split):
+def test_split_kv_dtypes_and_heads(api, cuda_device, dtype, heads, split, kernel):
     """The split path (pieces and the combine kernel) for fp16 inputs, for fewer than 128 heads,
     and with a caller's piece size on a batch the library would not split by itself."""
     if not tc_available():
@@ -339,7 +342,7 @@ def test_split_kv_dtypes_and_heads(api, cuda_device, dtype, heads, split):
     n = 6 if split == 0 else 48
     wl = W.make_workload(name="split_dt", q_lens=[1] * n, kv_lens=[3000 + 977 * i for i in range(n)], num_heads=heads,
                          topk=1024, seed=11, dtype=dtype, device=cuda_device)
-    out, lse = run(api, wl, "tc", cuda_device, split_tiles=split)
+    out, lse = run(api, wl, kernel, cuda_device, split_tiles=split)
     sample = [0, n // 2, n - 1]
     wl_c = wl.to("cpu")
     ref_out, ref_lse, _ = O.sparse_attn_sharedkv_oracle(
@@ -358,7 +361,7 @@ def test_rows_outside_every_request_are_zero(api, cuda_device, kernel):
     order: they must still come back as zero output and zero LSE, and the covered rows must
     equal the call without padding.  The output memory is poisoned first, so a row that no
     kernel writes shows up."""
-    if kernel == "tc" and not tc_available():
+    if kernel.startswith("tc") and not tc_available():
         pytest.skip("tensor-core path not built")
     from dsv4_planb_b200 import workloads as W
 
@@ -413,7 +416,7 @@ def test_rows_outside_every_request_are_zero(api, cuda_device, kernel):
 def test_misaligned_views_are_rehomed(api, cuda_device, kernel):
     """q and out views that start one element into an allocation (not 16-byte aligned) give the
     same bits as aligned tensors: the API copies q, and writes out through an aligned buffer."""
-    if kernel == "tc" and not tc_available():
+    if kernel.startswith("tc") and not tc_available():
         pytest.skip("tensor-core path not built")
     from dsv4_planb_b200 import workloads as W
 
@@ -440,7 +443,7 @@ def test_head_counts_off_the_q_box(api, cuda_device, kernel, heads, q_lens):
     """Head counts that are not a multiple of the 64-row Q box: with 16 heads and one token the
     box is taller than all of q (rows past the end read zeros); with 100 heads a token's second
     box reaches into the next token's rows (heads past N1 are computed and dropped)."""
-    if kernel == "tc" and not tc_available():
+    if kernel.startswith("tc") and not tc_available():
         pytest.skip("tensor-core path not built")
     from dsv4_planb_b200 import workloads as W
 
