@@ -543,9 +543,11 @@ def verify_gather(wl, out, lse, dev, rank, world, dist, n_sample):
     sinks = wl.sinks.float().contiguous()
     gathered = {}
     for name, tns in (("q", q_bits.contiguous()), ("keys", keys), ("meta", meta), ("sinks", sinks)):
-        lst = [torch.empty_like(tns) for _ in range(world)]
-        dist.all_gather(lst, tns)
-        gathered[name] = lst
+        # NCCL moves no int16: the bf16 / fp16 bit patterns travel as bfloat16 of the same bytes
+        wire = tns.view(torch.bfloat16) if tns.dtype == torch.int16 else tns
+        lst = [torch.empty_like(wire) for _ in range(world)]
+        dist.all_gather(lst, wire)
+        gathered[name] = [x.view(tns.dtype) for x in lst]
     if rank != 0:
         return None
     from oracle import golden_np as O

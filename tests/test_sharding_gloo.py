@@ -131,3 +131,57 @@ def test_dead_rank_is_detected_not_hung(tmp_path):
     assert ctx.processes[1].exitcode == 3
     res = torch.load(path)
     assert "error" in res  # rank 0's collective failed instead of waiting forever
+
+
+# dtypes torch's NCCL backend moves (int16 is not among them)
+NCCL_DTYPES = {torch.uint8, torch.int8, torch.int32, torch.int64, torch.float16, torch.bfloat16, torch.float32,
+               torch.float64, torch.bool}
+
+
+class _NcclDtypeCheck:
+    """torch.distributed as bench.py uses it, refusing what an NCCL process group refuses."""
+
+    ReduceOp = dist.ReduceOp
+
+    @staticmethod
+    def all_reduce(t, op=dist.ReduceOp.SUM):
+        assert t.dtype in NCCL_DTYPES, t.dtype
+        return dist.all_reduce(t, op=op)
+
+    @staticmethod
+    def all_gather(lst, t):
+        assert t.dtype in NCCL_DTYPES and all(x.dtype in NCCL_DTYPES for x in lst), t.dtype
+        return dist.all_gather(lst, t)
+
+
+def _verify_worker(rank, world, port, result_path):
+    import sys
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import bench
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    try:
+        # each rank has its own requests (different seeds and lengths), as under bench.py --gpus N
+        wl = W.make_workload(name=f"verify{rank}", q_lens=[1, 2, 1][: 2 + rank], kv_lens=[700, 1500, 900][: 2 + rank],
+                             num_heads=16, topk=128, seed=5 + rank)
+        out, lse = _oracle(wl)
+        res = bench.verify_gather(wl, out.to(torch.bfloat16), lse.float(), torch.device("cpu"), rank, world,
+                                  _NcclDtypeCheck, 3)
+        if rank == 0:
+            torch.save(res, result_path)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_bench_verify_gather_uses_nccl_dtypes(tmp_path):
+    """bench.py's multi-GPU verification gathers every rank's out / lse and sampled token inputs and
+    checks them against the oracle on rank 0.  Run over gloo with a wrapper that refuses the dtypes
+    NCCL refuses, on shards of different sizes: it must pass and report its check."""
+    port = _free_port()
+    path = str(tmp_path / "verify.pt")
+    mp.start_processes(_verify_worker, args=(2, port, path), nprocs=2, join=True, start_method="spawn")
+    res = torch.load(path)
+    assert res["parity_checked"] and res["pass"] and res["ranks"] == 2, res
