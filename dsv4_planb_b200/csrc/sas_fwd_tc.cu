@@ -1013,9 +1013,11 @@ done:
 //   warps 4-5  gather the CTA's own 32 key rows (all slabs) into the K ring
 //   warps 6-7  gather the other CTA's 32 keys' value slabs of this CTA into the PV operand ring
 //   warp 8     CTA 0: issues QK(j), then PV(j - 1), and the commits (multicast to both CTAs);
+//              CTA 1: tells CTA 0 when each of this CTA's K stages is complete;
 //              both: TMEM allocation (cta_group::2 needs the same warp in both CTAs)
 //   warp 9     copies the own keys' value slabs from the K ring into the PV operand ring; in CTA 1
-//              it also tells CTA 0 when this CTA's K and PV stages are complete
+//              it also tells CTA 0 when each PV stage is complete.  (K and PV completion are
+//              reported by different warps so that a late PV stage never holds back a K stage.)
 // ============================================================================================
 
 constexpr int kT2Threads = 320;
@@ -1029,7 +1031,7 @@ constexpr int kT2PStage = 64 * kBK * 2;                     // 64 heads x 64 key
 constexpr int kT2QTmemDims = 384;                           // Q dims in TMEM (A operand)
 constexpr int kT2QSmem = (kMaxDq - kT2QTmemDims) / 64 * 64 * 128;  // dims [384, 576): 3 slabs of 64 rows
 constexpr int kT2TmemO = 0, kT2TmemS = 256, kT2TmemQ = 320;
-constexpr uint32_t kT2TqReaders = 18;  // CTA 0: warps 0-3, 5-9; CTA 1: warps 0-7, 9
+constexpr uint32_t kT2TqReaders = 19;  // CTA 0: warps 0-3, 5-9; CTA 1: warps 0-9
 
 struct Hdr2 {
     uint64_t k_full[kT2KStages], k_empty[kT2KStages], k_peer[kT2KStages];
@@ -1069,6 +1071,33 @@ __device__ __forceinline__ void t2_rows(const TcArgs &p, const Item &it, const i
         dst[kt] = key_row(p, it, j, k0 + kt, fetched);
         fetched = j + 1 < it.j1 ? key_fetch(p, it, crow, j + 1, k0 + kt) : -1;
     }
+}
+
+// QK of one tile over the pair, NK = D_qk / 16 MMAs issued back to back (one thread).  Descriptors
+// advance by adding the byte offset / 16 to the start-address field (the shared window is below
+// 256 KiB, so the 14-bit field never carries).  A: dims [0, 384) from TMEM at `at`, the rest from
+// the shared-memory Q part (descriptor a0); B: the K stage (descriptor b0).
+template <int NK>
+__device__ __forceinline__ void t2_qk(uint32_t d, uint32_t at, uint64_t b0, uint64_t a0, uint32_t idesc) {
+#pragma unroll
+    for (int kk = 0; kk < NK; ++kk) {
+        const uint64_t bd = b0 + (uint64_t)(((kk >> 2) * kT2Slab + (kk & 3) * 32) >> 4);
+        if (kk < kT2QTmemDims / 16)
+            mma2_ts(d, at + kk * 8, bd, idesc, kk > 0 ? 1u : 0u);
+        else
+            mma2_ss(d, a0 + (uint64_t)((((kk - kT2QTmemDims / 16) >> 2) * (64 * 128) + (kk & 3) * 32) >> 4), bd,
+                    idesc, 1u);
+    }
+}
+
+// PV of one tile: O[:, 256 hf + ...] (+)= P x V over the pair, 2 x 4 MMAs of N = 256, K = 16 keys.
+__device__ __forceinline__ void t2_pv(uint32_t o, uint64_t pa0, uint64_t vb0, uint32_t idesc, bool first) {
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk)
+            mma2_ss(o + hf * 128, pa0 + (uint64_t)((kk * 32) >> 4),
+                    vb0 + (uint64_t)((hf * 2 * kT2VBlock + kk * 2048) >> 4), idesc, (!first || kk > 0) ? 1u : 0u);
 }
 
 template <bool kBF16, bool kSplit>
@@ -1143,6 +1172,12 @@ __global__ void __launch_bounds__(kT2Threads, 1)
             if (t < 0) break;
             const Item it = load_unit<kSplit>(p, t);
             if (it.skip) continue;
+            if (warp == 4 && lane == 0 && it.j1 > it.j0 && 64 * (int)rank < p.N1) {
+                // this CTA's heads of the unit's q rows, read by warps 0-3 when the unit starts
+                const int nh = min(64, p.N1 - 64 * (int)rank);
+                prefetch_l2_bulk(reinterpret_cast<const uint8_t *>(p.q) + ((int64_t)it.t * p.N1 + 64 * (int)rank) * p.Dq * 2,
+                                 (uint32_t)(nh * p.Dq * 2));
+            }
             const int32_t *crow = p.rows + (int64_t)it.t * p.row_cap;
             int32_t fetched = gt < kT2Half && it.j1 > it.j0 ? key_fetch(p, it, crow, it.j0, k0 + gt) : -1;
             for (int j = it.j0; j < it.j1; ++j, ++cnt) {
@@ -1195,7 +1230,6 @@ __global__ void __launch_bounds__(kT2Threads, 1)
             for (int j = it.j0; j < it.j1; ++j, ++kc, ++vc) {
                 const int ks = kc % kT2KStages, vs = vc % kT2VStages;
                 if (!wait_warp(sy, smem_u32(&hd->k_full[ks]), (kc / kT2KStages) & 1)) goto done;
-                if (rank == 1 && lane == 0) mbar_arrive_remote(map_to_cta(smem_u32(&hd->k_peer[ks]), 0));
                 if (!wait_warp(sy, smem_u32(&hd->v_empty[vs]), ((vc / kT2VStages) & 1) ^ 1, true)) goto done;
                 // four 4 KiB blocks (32 rows x 128 B each, the same swizzle phase at both places)
                 const uint8_t *ksrc = kring + (size_t)ks * kT2KStage;
@@ -1220,12 +1254,26 @@ __global__ void __launch_bounds__(kT2Threads, 1)
                 }
             }
         }
+    } else if (warp == 8 && rank != 0) {
+        // --------------- CTA 1: report each complete K stage to CTA 0 ---------------
+        uint32_t kc = 0;
+        for (uint32_t k = 0;; ++k) {
+            int t;
+            if (!tq_read(p, sy, rank, k, t)) goto done;
+            if (t < 0) break;
+            const Item it = load_unit<kSplit>(p, t);
+            if (it.skip) continue;
+            for (int j = it.j0; j < it.j1; ++j, ++kc) {
+                const int ks = kc % kT2KStages;
+                if (!wait_warp(sy, smem_u32(&hd->k_full[ks]), (kc / kT2KStages) & 1)) goto done;
+                if (lane == 0) mbar_arrive_remote(map_to_cta(smem_u32(&hd->k_peer[ks]), 0));
+            }
+        }
     } else if (warp == 8) {
         // ------------------------------ MMA (CTA 0) ------------------------------
-        if (rank != 0) goto done;
         const uint32_t idesc_s = idesc_f16(kBF16 ? 1u : 0u, 128, kBK, 0);
         const uint32_t idesc_o = idesc_f16(kBF16 ? 1u : 0u, 128, 256, 1);
-        const int nk = p.Dq / 16, nk_t = kT2QTmemDims / 16;
+        const int nk = p.Dq / 16;
         uint32_t kc = 0, sc = 0, vc = 0, qc = 0, oc = 0;
         for (uint32_t k = 0;; ++k) {
             int t;
@@ -1246,16 +1294,11 @@ __global__ void __launch_bounds__(kT2Threads, 1)
                     if (lane == 0) {
                         const uint32_t kb = smem_u32(kring + (size_t)ks * kT2KStage);
                         const uint32_t d = tmem + kT2TmemS + sb * kT2Half;
-                        for (int kk = 0; kk < nk; ++kk) {
-                            const uint64_t bdesc = sdesc_sw128(kb + (kk >> 2) * kT2Slab + (kk & 3) * 32, 16, 1024);
-                            if (kk < nk_t) {
-                                mma2_ts(d, tmem + kT2TmemQ + kk * 8, bdesc, idesc_s, kk > 0 ? 1u : 0u);
-                            } else {
-                                const uint64_t adesc =
-                                    sdesc_sw128(smem_u32(qs) + ((kk - nk_t) >> 2) * (64 * 128) + (kk & 3) * 32, 16, 1024);
-                                mma2_ss(d, adesc, bdesc, idesc_s, 1u);
-                            }
-                        }
+                        const uint64_t b0 = sdesc_sw128(kb, 16, 1024), a0 = sdesc_sw128(smem_u32(qs), 16, 1024);
+                        if (nk == 36)
+                            t2_qk<36>(d, tmem + kT2TmemQ, b0, a0, idesc_s);
+                        else
+                            t2_qk<32>(d, tmem + kT2TmemQ, b0, a0, idesc_s);
                         tc2_commit_mc(smem_u32(&hd->s_full[sb]), 3);
                         tc2_commit_mc(smem_u32(&hd->k_empty[ks]), 3);
                     }
@@ -1276,11 +1319,8 @@ __global__ void __launch_bounds__(kT2Threads, 1)
                         const bool stall = p.test_stall && vc == 0;  // test hook, see SAS_FWD_FLAG_TEST_STALL
                         const uint32_t pa = smem_u32(pring + (size_t)ps * kT2PStage);
                         const uint32_t vb = smem_u32(vring + (size_t)vs * kT2VStage);
-                        for (int hf = 0; hf < 2; ++hf)
-                            for (int kk = 0; kk < kBK / 16; ++kk)
-                                mma2_ss(tmem + kT2TmemO + hf * 128, sdesc_sw128(pa + kk * 32, 16, 1024),
-                                        sdesc_sw128(vb + hf * 2 * kT2VBlock + kk * 2048, kT2VBlock, 1024), idesc_o,
-                                        (!first || kk > 0) ? 1u : 0u);
+                        t2_pv(tmem + kT2TmemO, sdesc_sw128(pa, 16, 1024), sdesc_sw128(vb, kT2VBlock, 1024), idesc_o,
+                              first);
                         if (!stall) tc2_commit_mc(smem_u32(&hd->p_free[ps]), 3);
                         tc2_commit_mc(smem_u32(&hd->v_empty[vs]), 3);
                         tc2_commit_mc(smem_u32(&hd->pv_done), 3);
@@ -1336,12 +1376,19 @@ __global__ void __launch_bounds__(kT2Threads, 1)
                     }
                     tmem_st32(tmem + lane_base + kT2TmemQ + c * 32, w);
                 }
-                const int nq = (p.Dq - kT2QTmemDims) / 8;  // 16-byte chunks of the smem part
-                for (int c = half * (nq / 2); c < (half + 1) * (nq / 2); ++c) {
-                    const int s = c >> 3, cc = c & 7;
-                    const uint4 x = hv ? __ldg(qrow + kT2QTmemDims / 8 + c) : make_uint4(0, 0, 0, 0);
-                    *reinterpret_cast<uint4 *>(qs + s * (64 * 128) + (r >> 3) * 1024 + (r & 7) * 128 +
-                                               ((cc ^ (r & 7)) << 4)) = x;
+                // the smem part: (D_qk - 384) / 8 16-byte chunks, half of them per thread, loads first
+                constexpr int kQh = (kMaxDq - kT2QTmemDims) / 16;
+                const int nqh = (p.Dq - kT2QTmemDims) / 16;
+                uint4 xq[kQh];
+#pragma unroll
+                for (int e = 0; e < kQh; ++e)
+                    xq[e] = hv && e < nqh ? __ldg(qrow + kT2QTmemDims / 8 + half * nqh + e) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+                for (int e = 0; e < kQh; ++e) {
+                    const int c = half * nqh + e, s = c >> 3, cc = c & 7;
+                    if (e < nqh)
+                        *reinterpret_cast<uint4 *>(qs + s * (64 * 128) + (r >> 3) * 1024 + (r & 7) * 128 +
+                                                   ((cc ^ (r & 7)) << 4)) = xq[e];
                 }
                 tc_wait_st();
                 fence_proxy_async_smem();

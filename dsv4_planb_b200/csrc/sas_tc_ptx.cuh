@@ -81,6 +81,10 @@ __device__ __forceinline__ bool mbar_try_cluster(uint32_t bar, uint32_t parity) 
 }
 
 // Fetch the 128-byte line holding `ptr` into L2 (no data returned to the SM).
+// Bulk prefetch of [ptr, ptr + bytes) into L2 (ptr 16-byte aligned, bytes a multiple of 16).
+__device__ __forceinline__ void prefetch_l2_bulk(const void *ptr, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(ptr), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ void prefetch_l2(const void *ptr) {
     asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
 }
