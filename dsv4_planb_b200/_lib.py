@@ -44,6 +44,7 @@ EXPORTS = (
     "sas_forward_kernel_count",
     "sas_forward",
     "sas_forward_noalloc",
+    "sas_backward",
     "sas_noalloc_read_status",
     "sas_resolve_rows",
     "sas_split_plan",
@@ -127,6 +128,7 @@ _SIGNATURES = {
     "sas_forward": (ctypes.c_int, [ctypes.POINTER(SasFwdArgs)] + [_P] * 13 + [_P, _SZ, _P]),
     "sas_forward_noalloc": (ctypes.c_int, [ctypes.POINTER(SasFwdArgs)] + [_P] * 13 + [_P]),
     "sas_noalloc_read_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), _P]),
+    "sas_backward": (ctypes.c_int, [ctypes.POINTER(SasFwdArgs)] + [_P] * 18 + [_P, _SZ, _P]),
     "sas_resolve_rows": (ctypes.c_int, [ctypes.POINTER(SasFwdArgs)] + [_P] * 8 + [_P, _SZ, _P]),
     "sas_split_plan": (ctypes.c_int, [ctypes.POINTER(SasFwdArgs), ctypes.POINTER(ctypes.c_int32),
                                       ctypes.POINTER(ctypes.c_int32)]),

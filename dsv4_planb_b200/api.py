@@ -24,7 +24,7 @@ Differences, all widenings of the reference contract:
 * no host synchronisation: scenario 2 (CFA) takes each token's compressed range
   from the block table on the device (the reference reads ``seqused_kv.max()``
   on the host, api.py:260), and TND needs none once ``max_seqlen_q`` is given;
-* extra keywords ``kernel`` ("auto" | "simt" | "tc"), ``max_seqlen_q`` (skips
+* extra keywords ``kernel`` ("auto" | "simt" | "tc" | "tc2"), ``max_seqlen_q`` (skips
   the host read of ``cu_seqlens_q``), ``out`` / ``lse_out`` (preallocated
   outputs), ``check_status`` (read the device status word, synchronising),
   ``split_tiles`` and ``lazy_rescale``.
@@ -95,11 +95,18 @@ def _out_shapes(q: torch.Tensor, layout_q: str, v_head_dim: int):
     return (B, S, N1, v_head_dim), (B, S, N1)
 
 
-def _launch(q, ori_kv, cmp_kv, cmp_sparse_indices, ori_block_table, cmp_block_table, cu_seqlens_q, seqused_kv,
-            sinks, metadata, softmax_scale, cmp_ratio, ori_win_left, layout_q, v_head_dim, kernel, max_seqlen_q,
-            split_tiles, check_status, lazy_rescale, out, lse_out):
-    """Marshal one sas_forward call (the body of both registered ops).  ``out`` / ``lse_out`` are the
-    outputs in the layout of ``q``; ``max_seqlen_q`` < 0 reads it from ``cu_seqlens_q`` (host sync)."""
+class _Call:
+    """The device arguments of one call, as sas_forward and sas_backward take them."""
+
+    __slots__ = ("args", "lib", "ws", "q", "ori_kv", "ori_bt", "cmp_kv", "cmp_bt", "idx", "q_prefix", "act_q",
+                 "seq_kv", "sinks", "metadata", "T", "N1", "Dv", "stream")
+
+
+def _marshal(q, ori_kv, cmp_kv, cmp_sparse_indices, ori_block_table, cmp_block_table, cu_seqlens_q, seqused_kv,
+             sinks, metadata, softmax_scale, cmp_ratio, ori_win_left, layout_q, v_head_dim, kernel, max_seqlen_q,
+             split_tiles, lazy_rescale) -> _Call:
+    """Flatten the layouts, check the shapes and fill SasFwdArgs; ``max_seqlen_q`` < 0 reads it from
+    ``cu_seqlens_q`` (host sync).  Allocates the call's workspace."""
     dev = q.device
     scenario = _scenario(cmp_kv, cmp_sparse_indices)
     if layout_q == "TND":
@@ -187,41 +194,60 @@ def _launch(q, ori_kv, cmp_kv, cmp_sparse_indices, ori_block_table, cmp_block_ta
     lib = _lib.load()
     nbytes = _lib.ctypes.c_size_t(0)
     _lib.check(lib.sas_workspace_size(_lib.ctypes.byref(args), _lib.ctypes.byref(nbytes)), "sas_workspace_size")
-    ws = _workspace(nbytes.value, dev)
+    c = _Call()
+    c.args, c.lib, c.ws = args, lib, _workspace(nbytes.value, dev)
+    c.q, c.ori_kv, c.ori_bt, c.cmp_kv, c.cmp_bt, c.idx = _dense16(q_flat), ori_kv_d, ori_bt, cmp_kv_d, cmp_bt, idx_flat
+    c.q_prefix, c.act_q, c.seq_kv, c.sinks, c.metadata = q_prefix, act_q, seq_kv, sinks_d, metadata
+    c.T, c.N1, c.Dv = T, N1, Dv
+    c.stream = torch.cuda.current_stream(dev).cuda_stream
+    return c
+
+
+def _check_status(c: _Call, what: str) -> None:
+    st = _lib.ctypes.c_uint32(0)
+    _lib.check(c.lib.sas_read_status(_ptr(c.ws), _lib.ctypes.byref(st), c.stream), "sas_read_status")
+    if st.value:
+        raise RuntimeError(f"{what} device status: {_lib.status_names(st.value)}")
+
+
+def _launch(q, ori_kv, cmp_kv, cmp_sparse_indices, ori_block_table, cmp_block_table, cu_seqlens_q, seqused_kv,
+            sinks, metadata, softmax_scale, cmp_ratio, ori_win_left, layout_q, v_head_dim, kernel, max_seqlen_q,
+            split_tiles, check_status, lazy_rescale, out, lse_out):
+    """One sas_forward call (the body of both registered forward ops).  ``out`` / ``lse_out`` are
+    the outputs in the layout of ``q``."""
+    c = _marshal(q, ori_kv, cmp_kv, cmp_sparse_indices, ori_block_table, cmp_block_table, cu_seqlens_q, seqused_kv,
+                 sinks, metadata, softmax_scale, cmp_ratio, ori_win_left, layout_q, v_head_dim, kernel, max_seqlen_q,
+                 split_tiles, lazy_rescale)
+    T, N1, Dv = c.T, c.N1, c.Dv
     out_flat = out.view(T, N1, Dv)
     out_user = None  # a caller's out that starts inside a 16-byte vector: written through a copy
     if out_flat.data_ptr() % 16:
         out_user, out_flat = out_flat, torch.empty_like(out_flat)
     lse_flat = lse_out.view(T, N1)
-    q_c = _dense16(q_flat)
-    stream = torch.cuda.current_stream(dev).cuda_stream
-    rc = lib.sas_forward(
-        _lib.ctypes.byref(args),
-        _ptr(q_c),
-        _ptr(ori_kv_d),
-        _ptr(ori_bt),
-        _ptr(cmp_kv_d),
-        _ptr(cmp_bt),
-        _ptr(idx_flat),
-        _ptr(q_prefix),
-        _ptr(act_q),
-        _ptr(seq_kv),
-        _ptr(sinks_d),
-        _ptr(metadata),
+    rc = c.lib.sas_forward(
+        _lib.ctypes.byref(c.args),
+        _ptr(c.q),
+        _ptr(c.ori_kv),
+        _ptr(c.ori_bt),
+        _ptr(c.cmp_kv),
+        _ptr(c.cmp_bt),
+        _ptr(c.idx),
+        _ptr(c.q_prefix),
+        _ptr(c.act_q),
+        _ptr(c.seq_kv),
+        _ptr(c.sinks),
+        _ptr(c.metadata),
         _ptr(out_flat),
         _ptr(lse_flat),
-        _ptr(ws),
-        ws.numel(),
-        stream,
+        _ptr(c.ws),
+        c.ws.numel(),
+        c.stream,
     )
     _lib.check(rc, "sas_forward")
     if out_user is not None:
         out_user.copy_(out_flat)
     if check_status:
-        st = _lib.ctypes.c_uint32(0)
-        _lib.check(lib.sas_read_status(_ptr(ws), _lib.ctypes.byref(st), stream), "sas_read_status")
-        if st.value:
-            raise RuntimeError(f"sas_forward device status: {_lib.status_names(st.value)}")
+        _check_status(c, "sas_forward")
 
 
 @torch.library.custom_op("sas_b200::sparse_attn_sharedkv", mutates_args=(), device_types="cuda")
@@ -269,6 +295,82 @@ def _op_out_fake(q, ori_kv, cmp_kv, cmp_sparse_indices, ori_block_table, cmp_blo
     return None
 
 
+def _launch_backward(q, ori_kv, cmp_kv, cmp_sparse_indices, ori_block_table, cmp_block_table, cu_seqlens_q,
+                     seqused_kv, sinks, out, lse, grad_out, grad_lse, softmax_scale, cmp_ratio, ori_win_left,
+                     layout_q, v_head_dim, max_seqlen_q, check_status):
+    """One sas_backward call: (dq, d_ori_kv, d_cmp_kv, d_sinks) in the inputs' shapes and dtypes
+    (d_cmp_kv empty when there is no compressed cache)."""
+    c = _marshal(q, ori_kv, cmp_kv, cmp_sparse_indices, ori_block_table, cmp_block_table, cu_seqlens_q, seqused_kv,
+                 sinks, None, softmax_scale, cmp_ratio, ori_win_left, layout_q, v_head_dim, "simt", max_seqlen_q, 0,
+                 False)
+    dev, T, N1, Dv, D = q.device, c.T, c.N1, c.Dv, q.shape[-1]
+    dq = torch.empty((T, N1, D), dtype=torch.float32, device=dev)
+    d_ori = torch.zeros(ori_kv.shape, dtype=torch.float32, device=dev)
+    d_cmp = (torch.zeros(cmp_kv.shape, dtype=torch.float32, device=dev) if cmp_kv is not None
+             else torch.zeros(0, dtype=torch.float32, device=dev))
+    d_sinks = torch.zeros(N1, dtype=torch.float32, device=dev)
+    out_c = _dense16(out.reshape(T, N1, Dv))
+    lse_c = lse.reshape(T, N1).to(torch.float32).contiguous()
+    dout_c = _dense16(grad_out.reshape(T, N1, Dv).to(q.dtype))
+    dlse_c = None if grad_lse is None else grad_lse.reshape(T, N1).to(torch.float32).contiguous()
+    rc = c.lib.sas_backward(
+        _lib.ctypes.byref(c.args), _ptr(c.q), _ptr(c.ori_kv), _ptr(c.ori_bt), _ptr(c.cmp_kv), _ptr(c.cmp_bt),
+        _ptr(c.idx), _ptr(c.q_prefix), _ptr(c.act_q), _ptr(c.seq_kv), _ptr(c.sinks), _ptr(out_c), _ptr(lse_c),
+        _ptr(dout_c), _ptr(dlse_c), _ptr(dq), _ptr(d_ori), _ptr(d_cmp if cmp_kv is not None else None),
+        _ptr(d_sinks), _ptr(c.ws), c.ws.numel(), c.stream)
+    _lib.check(rc, "sas_backward")
+    if check_status:
+        _check_status(c, "sas_backward")
+    return (dq.view(q.shape).to(q.dtype), d_ori.to(ori_kv.dtype),
+            d_cmp.to(cmp_kv.dtype) if cmp_kv is not None else d_cmp, d_sinks.to(sinks.dtype))
+
+
+@torch.library.custom_op("sas_b200::sparse_attn_sharedkv_backward", mutates_args=(), device_types="cuda")
+def _op_bwd(q: torch.Tensor, ori_kv: torch.Tensor, cmp_kv: Optional[torch.Tensor],
+            cmp_sparse_indices: Optional[torch.Tensor], ori_block_table: torch.Tensor,
+            cmp_block_table: Optional[torch.Tensor], cu_seqlens_q: Optional[torch.Tensor], seqused_kv: torch.Tensor,
+            sinks: torch.Tensor, out: torch.Tensor, lse: torch.Tensor, grad_out: torch.Tensor,
+            grad_lse: Optional[torch.Tensor], softmax_scale: float, cmp_ratio: int, ori_win_left: int,
+            layout_q: str, v_head_dim: int, max_seqlen_q: int,
+            check_status: bool) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Gradients of sparse_attn_sharedkv with respect to q, ori_kv, cmp_kv and sinks."""
+    return _launch_backward(q, ori_kv, cmp_kv, cmp_sparse_indices, ori_block_table, cmp_block_table, cu_seqlens_q,
+                            seqused_kv, sinks, out, lse, grad_out, grad_lse, softmax_scale, cmp_ratio, ori_win_left,
+                            layout_q, v_head_dim, max_seqlen_q, check_status)
+
+
+@_op_bwd.register_fake
+def _op_bwd_fake(q, ori_kv, cmp_kv, cmp_sparse_indices, ori_block_table, cmp_block_table, cu_seqlens_q, seqused_kv,
+                 sinks, out, lse, grad_out, grad_lse, softmax_scale, cmp_ratio, ori_win_left, layout_q, v_head_dim,
+                 max_seqlen_q, check_status):
+    d_cmp = cmp_kv.new_empty(cmp_kv.shape) if cmp_kv is not None else q.new_empty(0, dtype=torch.float32)
+    return q.new_empty(q.shape), ori_kv.new_empty(ori_kv.shape), d_cmp, sinks.new_empty(sinks.shape)
+
+
+def _setup_context(ctx, inputs, output):
+    (q, ori_kv, cmp_kv, cmp_sparse_indices, ori_block_table, cmp_block_table, cu_seqlens_q, seqused_kv, sinks,
+     _metadata, softmax_scale, cmp_ratio, ori_win_left, layout_q, v_head_dim, _kernel, max_seqlen_q, _split,
+     check_status, _lazy) = inputs
+    out, lse = output
+    ctx.save_for_backward(q, ori_kv, cmp_kv, cmp_sparse_indices, ori_block_table, cmp_block_table, cu_seqlens_q,
+                          seqused_kv, sinks, out, lse)
+    ctx.consts = (softmax_scale, cmp_ratio, ori_win_left, layout_q, v_head_dim, max_seqlen_q, check_status)
+    ctx.has_cmp = cmp_kv is not None
+
+
+def _backward(ctx, grad_out, grad_lse):
+    q, ori_kv, cmp_kv, idx, ori_bt, cmp_bt, cu, seqused_kv, sinks, out, lse = ctx.saved_tensors
+    if grad_out is None:
+        grad_out = torch.zeros_like(out)
+    dq, d_ori, d_cmp, d_sinks = torch.ops.sas_b200.sparse_attn_sharedkv_backward(
+        q, ori_kv, cmp_kv, idx, ori_bt, cmp_bt, cu, seqused_kv, sinks, out, lse, grad_out, grad_lse, *ctx.consts)
+    return (dq, d_ori, d_cmp if ctx.has_cmp else None, None, None, None, None, None, d_sinks) + (None,) * 11
+
+
+# the op with op-owned outputs is differentiable (q, ori_kv, cmp_kv, sinks); the ``_out`` form is not
+torch.library.register_autograd("sas_b200::sparse_attn_sharedkv", _backward, setup_context=_setup_context)
+
+
 def sparse_attn_sharedkv(
     q: torch.Tensor,
     *,
@@ -310,7 +412,7 @@ def sparse_attn_sharedkv(
     ``return_softmax_lse`` also the fp32 natural-log LSE ``[T, N1]`` (TND) or
     ``[B, S, N1]`` (BSND) with the sink folded in.
 
-    B200 extensions of the reference signature: ``kernel`` ("auto", "tc", "simt"),
+    B200 extensions of the reference signature: ``kernel`` ("auto", "tc", "tc2", "simt"),
     ``max_seqlen_q`` (no host synchronisation when given), ``out`` / ``lse_out``
     (caller-owned outputs), ``check_status`` (raise on device-side status bits) and
     ``split_tiles`` (piece size, in 64-key tiles, for cutting long tokens across the
@@ -319,6 +421,8 @@ def sparse_attn_sharedkv(
     threshold, faster, P rounded at another scale than the golden's; off by default).
     Everything here is shape logic that ``torch.compile`` traces; the launch is the
     registered op ``torch.ops.sas_b200.sparse_attn_sharedkv`` (``..._out`` with ``out``).
+    Without ``out`` / ``lse_out`` the call is differentiable in q, ori_kv, cmp_kv and sinks
+    (``sas_backward``, CUDA cores; the reference has no backward).
     """
     del seqused_q, core_num  # API parity (the reference kernel does not read them either)
     assert ori_mask_mode == 4, "only ori_mask_mode=4 supported"

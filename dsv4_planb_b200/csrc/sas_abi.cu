@@ -28,6 +28,10 @@ int launch_split_metadata(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws
 int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const void *q, const void *ori_kv,
                   const int32_t *ori_bt, const void *cmp_kv, const int32_t *cmp_bt, const float *sinks, void *out,
                   float *lse, cudaStream_t s, bool pair);
+int launch_bwd_simt(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const void *q, const void *ori_kv,
+                    const int32_t *ori_bt, const void *cmp_kv, const int32_t *cmp_bt, const float *sinks,
+                    const void *out, const float *lse, const void *dout, const float *dlse, float *dq, float *d_ori,
+                    float *d_cmp, float *d_sinks, cudaStream_t s);
 
 int check_cuda(cudaError_t e) {
     if (e == cudaSuccess) return SAS_OK;
@@ -197,6 +201,39 @@ int sas_forward(const SasFwdArgs *args, const void *q, const void *ori_kv, const
     else rc = launch_fwd_simt(a, L, ws, q, ori_kv, ori_block_table, cmp_kv, cmp_block_table, sinks, out, lse, s);
     if (rc) return rc;
     return record_kernel_event(false, s);
+}
+
+int sas_backward(const SasFwdArgs *args, const void *q, const void *ori_kv, const int32_t *ori_block_table,
+                 const void *cmp_kv, const int32_t *cmp_block_table, const int32_t *cmp_indices,
+                 const int32_t *q_prefix, const int32_t *act_q_len, const int32_t *act_kv_len, const float *sinks,
+                 const void *out, const float *lse, const void *dout, const float *dlse, float *dq,
+                 float *d_ori_kv, float *d_cmp_kv, float *d_sinks, void *workspace, size_t workspace_bytes,
+                 void *stream) {
+    if (!args) return SAS_ERR_INVALID_ARG;
+    const SasFwdArgs &a = *args;
+    int rc = validate_fwd(a);
+    if (rc) return rc;
+    if (a.head_dim > 1024) return SAS_ERR_UNSUPPORTED;
+    rc = check_inputs(a, ori_kv, ori_block_table, cmp_kv, cmp_block_table, cmp_indices, q_prefix, act_q_len,
+                      act_kv_len);
+    if (rc) return rc;
+    if (a.num_tokens > 0 && (!q || !out || !lse || !dout || !sinks || !dq || !d_ori_kv || !d_sinks))
+        return SAS_ERR_INVALID_ARG;
+    if (a.num_tokens > 0 && a.scenario >= 2 && !d_cmp_kv) return SAS_ERR_INVALID_ARG;
+    const sas::FwdLayout L = fwd_layout(a);
+    if (!workspace || workspace_bytes < L.total) return SAS_ERR_WORKSPACE;
+    rc = check_alignment(q, ori_kv, ori_block_table, cmp_kv, cmp_block_table, cmp_indices, q_prefix, act_q_len,
+                         act_kv_len, sinks, out, lse, workspace);
+    if (rc) return rc;
+    if (!aligned(dout, 16) || !aligned(dq, 16) || !aligned(dlse, 4) || !aligned(d_ori_kv, 4) ||
+        !aligned(d_cmp_kv, 4) || !aligned(d_sinks, 4))
+        return SAS_ERR_INVALID_ARG;
+    char *ws = static_cast<char *>(workspace);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    rc = launch_prep(a, L, ws, cmp_block_table, cmp_indices, q_prefix, act_q_len, act_kv_len, s);
+    if (rc) return rc;
+    return launch_bwd_simt(a, L, ws, q, ori_kv, ori_block_table, cmp_kv, cmp_block_table, sinks, out, lse, dout,
+                           dlse, dq, d_ori_kv, d_cmp_kv, d_sinks, s);
 }
 
 int sas_set_kernel_events(void *start_event, void *stop_event) {

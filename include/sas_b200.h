@@ -177,6 +177,32 @@ int sas_forward(const SasFwdArgs *args, const void *q, const void *ori_kv, const
                 size_t workspace_bytes, void *stream);
 
 /*
+ * Backward pass (no counterpart in the reference, which has none,
+ * test_graph_mode.py:314-324).  Same arguments as sas_forward up to sinks,
+ * then the forward's out and lse, the gradient of out (dout, the layout and
+ * dtype of out) and optionally of lse (dlse, fp32 [T][N1], NULL = zero), and
+ * the gradients:
+ *   dq        fp32 [T][N1][D_qk], written;
+ *   d_ori_kv  fp32 [ori_block_num * ori_block_size][D_qk], added into;
+ *   d_cmp_kv  fp32 [cmp_block_num * cmp_block_size][D_qk], added into
+ *             (scenarios 2 and 3; may be NULL in scenario 1);
+ *   d_sinks   fp32 [N1], added into.
+ * K = V share a row, so a row's gradient holds its key and its value parts.
+ * Rows are shared across tokens and heads and their gradients are summed with
+ * atomics: the order of the sum, and so the last bits, vary between calls.
+ * The softmax weights are differentiated exactly (the forward's rounding of P
+ * to the input dtype is not).  Runs on CUDA cores for every shape with
+ * D_qk <= 1024; args->kernel is ignored.  The workspace is sas_forward's
+ * (sas_workspace_size).  dout and dq need 16-byte aligned bases.
+ */
+int sas_backward(const SasFwdArgs *args, const void *q, const void *ori_kv, const int32_t *ori_block_table,
+                 const void *cmp_kv, const int32_t *cmp_block_table, const int32_t *cmp_indices,
+                 const int32_t *q_prefix, const int32_t *act_q_len, const int32_t *act_kv_len, const float *sinks,
+                 const void *out, const float *lse, const void *dout, const float *dlse, float *dq,
+                 float *d_ori_kv, float *d_cmp_kv, float *d_sinks, void *workspace, size_t workspace_bytes,
+                 void *stream);
+
+/*
  * Index-handling export: runs only the key-resolution step of sas_forward and
  * copies, per flat token row, {b, s_global, ori_left, n_win, n_cmp, valid}
  * into token_info[T][8] (int32) and the physical compressed rows

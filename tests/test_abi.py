@@ -310,3 +310,46 @@ def test_split_plan_shape_matches_the_workspace(lib):
         a.split_tiles = 6
         P, M = plan(a)
         assert M == 6 and P == -(-34 // 6)
+
+
+def test_backward_op_fake_shapes():
+    # The backward op's fake implementation: gradients in the shapes and dtypes of q, the pools and
+    # the sinks (an empty fp32 tensor for the compressed pool when there is none).
+    import torch
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    import dsv4_planb_b200.api  # noqa: F401  (registers the ops)
+
+    with FakeTensorMode():
+        q = torch.empty(6, 128, 576, dtype=torch.bfloat16)
+        pool = torch.empty(10, 128, 1, 576, dtype=torch.bfloat16)
+        bt = torch.empty(2, 5, dtype=torch.int32)
+        idx = torch.empty(6, 1, 2048, dtype=torch.int32)
+        cu = torch.empty(3, dtype=torch.int32)
+        kv = torch.empty(2, dtype=torch.int32)
+        sinks = torch.empty(128, dtype=torch.float32)
+        out = torch.empty(6, 128, 512, dtype=torch.bfloat16)
+        lse = torch.empty(6, 128, dtype=torch.float32)
+        dq, d_ori, d_cmp, d_s = torch.ops.sas_b200.sparse_attn_sharedkv_backward(
+            q, pool, pool, idx, bt, bt, cu, kv, sinks, out, lse, out, lse, 0.04, 4, 127, "TND", 512, 3, False)
+        assert dq.shape == q.shape and dq.dtype == q.dtype
+        assert d_ori.shape == pool.shape and d_cmp.shape == pool.shape and d_s.shape == sinks.shape
+        dq, d_ori, d_cmp, d_s = torch.ops.sas_b200.sparse_attn_sharedkv_backward(
+            q, pool, None, None, bt, None, cu, kv, sinks, out, lse, out, None, 0.04, 4, 127, "TND", 512, 3, False)
+        assert d_cmp.numel() == 0 and d_ori.shape == pool.shape
+
+
+def test_backward_rejects_bad_pointers(lib):
+    # sas_backward checks its pointers before any device work: a missing or misaligned gradient
+    # buffer and a short workspace are argument errors.
+    a = good_args()
+    base = [0x10000 * (i + 1) for i in range(18)]  # q .. d_sinks, all 256-byte aligned
+    for i, off in [(12, 8), (14, 8), (15, 2), (17, 2), (16, 2)]:  # dout, dq, d_ori, d_sinks, d_cmp
+        ptrs = list(base)
+        ptrs[i] += off
+        assert lib.sas_backward(ctypes.byref(a), *ptrs, 0x1000000, 1 << 30, None) == _lib.SAS_ERR_INVALID_ARG, i
+    for i in (10, 11, 12, 14, 15, 17):  # out, lse, dout, dq, d_ori, d_sinks are required
+        ptrs = list(base)
+        ptrs[i] = None
+        assert lib.sas_backward(ctypes.byref(a), *ptrs, 0x1000000, 1 << 30, None) == _lib.SAS_ERR_INVALID_ARG, i
+    assert lib.sas_backward(ctypes.byref(a), *base, 0x1000000, 16, None) == _lib.SAS_ERR_WORKSPACE
