@@ -141,3 +141,28 @@ def test_backward_unmapped_blocks_and_tensor_core_forward(cuda_device):
     wl.ori_block_table[0, 7] = -1
     wl.cmp_block_table[1, 0] = -1
     _run(wl, kernel="tc")
+
+
+def test_backward_bsnd_matches_tnd(cuda_device):
+    """The BSND layout (q [B, S, N1, D], indices [B, S, 1, K]) gives the TND call's gradients."""
+    wl = W.make_workload(name="bwdbsnd", q_lens=[2, 2], kv_lens=[900, 2100], num_heads=32, topk=128, seed=47,
+                         device=cuda_device)
+    kw = wl.api_kwargs()
+    grads = []
+    for layout in ("TND", "BSND"):
+        q = wl.q.detach().clone()
+        idx = kw["cmp_sparse_indices"]
+        if layout == "BSND":
+            q = q.reshape(2, 2, *q.shape[1:])
+            idx = idx.reshape(2, 2, *idx.shape[1:])
+        q.requires_grad_(True)
+        ori = wl.ori_kv.detach().clone().requires_grad_(True)
+        cmp = wl.cmp_kv.detach().clone().requires_grad_(True)
+        sinks = wl.sinks.detach().clone().requires_grad_(True)
+        args = dict(kw, ori_kv=ori, cmp_kv=cmp, sinks=sinks, cmp_sparse_indices=idx, layout_q=layout)
+        out = sparse_attn_sharedkv(q, check_status=True, **args)
+        g = torch.ones_like(out)
+        out.backward(g)
+        grads.append((q.grad.reshape(wl.q.shape).float(), ori.grad.float(), cmp.grad.float(), sinks.grad.float()))
+    for name, a, b in zip(("dq", "d_ori_kv", "d_cmp_kv", "d_sinks"), *grads):
+        assert float((a - b).abs().max()) <= 1e-3 * float(b.abs().max()) + 1e-6, name
