@@ -143,6 +143,12 @@ static_assert(sizeof(Hdr) <= kDataOff, "header must fit before the data area");
 constexpr int kScoreSmem = kDataOff + kKStages * (kMaxDq / 64) * kChunkBytes;
 constexpr int kOutSmem = kDataOff + kVStages * (kMaxDv / 64) * kChunkBytes + kPStages * kMsgBytes;
 constexpr int kSmemBytes = (kScoreSmem > kOutSmem ? kScoreSmem : kOutSmem) + 1024;  // + alignment slack
+// Output CTA epilogue staging, after its V and P rings: per epilogue warp two slabs of 64 columns
+// of O for its 32 head rows (SW128 rows of 128 bytes), each written out by one TMA store.
+constexpr int kOutStageOff = kOutSmem;                  // from the aligned base of shared memory
+constexpr int kOutWarpSlab = 32 * 128;
+static_assert(kOutStageOff % 1024 == 0, "the staging slabs need 1 KiB alignment (128-byte swizzle)");
+static_assert(kOutStageOff + 4 * 2 * kOutWarpSlab + 1024 <= kSmemBytes, "the staging fits the launch's shared memory");
 
 struct TcArgs {
     const void *q;
@@ -508,7 +514,8 @@ __device__ void write_partial(const TcArgs &p, const Hdr *hd, const Item &it, ui
 template <bool kBF16, bool kSplit>
 __global__ void __launch_bounds__(kThreads, 1)
     fwd_tc_kernel(const TcArgs p, const __grid_constant__ CUtensorMap ori_map,
-                  const __grid_constant__ CUtensorMap cmp_map, const __grid_constant__ CUtensorMap q_map) {
+                  const __grid_constant__ CUtensorMap cmp_map, const __grid_constant__ CUtensorMap q_map,
+                  const __grid_constant__ CUtensorMap out_map) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     Hdr *hd = reinterpret_cast<Hdr *>(smem);
@@ -947,7 +954,47 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!wait_warp(sy, smem_u32(&hd->fin_ready), frc & 1)) goto done;
                 ++frc;
                 tc_fence_after();
-                if (it.np == 1) {
+                if (it.np == 1 && p.N1 % 32 == 0) {
+                    // O / lr, 64 columns at a time: each warp stages its 32 head rows (128-byte
+                    // swizzled rows) and writes them with one TMA store, two slabs in flight per warp
+                    if (warp * 32 < p.N1) {
+                        const float inv = 1.f / hd->fin_l[h];
+                        const uint32_t stage0 = smem_u32(smem + kOutStageOff) + warp * 2 * kOutWarpSlab;
+                        for (int sl = 0; sl < p.Dv / 64; ++sl) {
+                            const uint32_t buf = stage0 + (sl & 1) * kOutWarpSlab;
+                            if (lane == 0) bulk_wait_read<1>();  // the store two slabs back has read buf
+                            __syncwarp();
+                            uint32_t r0[32], r1[32];
+                            tmem_ld32(tmem + lane_base + sl * 64, r0);
+                            tmem_ld32(tmem + lane_base + sl * 64 + 32, r1);
+                            tc_wait_ld();
+#pragma unroll
+                            for (int cc = 0; cc < 8; ++cc) {
+                                uint32_t w[4];
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) {
+                                    const int k = 8 * (cc & 3) + 2 * e;
+                                    const float a = __uint_as_float(cc < 4 ? r0[k] : r1[k]) * inv;
+                                    const float b = __uint_as_float(cc < 4 ? r0[k + 1] : r1[k + 1]) * inv;
+                                    if constexpr (kBF16) {
+                                        __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+                                        w[e] = *reinterpret_cast<uint32_t *>(&v);
+                                    } else {
+                                        __half2 v = __floats2half2_rn(a, b);
+                                        w[e] = *reinterpret_cast<uint32_t *>(&v);
+                                    }
+                                }
+                                st_shared_v4(buf + lane * 128 + ((cc ^ (lane & 7)) << 4), w[0], w[1], w[2], w[3]);
+                            }
+                            fence_proxy_async_smem();
+                            __syncwarp();
+                            if (lane == 0) {
+                                tma_store_2d(&out_map, buf, sl * 64, t * p.N1 + warp * 32);
+                                bulk_commit();
+                            }
+                        }
+                    }
+                } else if (it.np == 1) {
                     const float inv = 1.f / hd->fin_l[h];
                     for (int c = 0; c < p.Dv / 32; ++c) {
                         uint32_t r[32];
@@ -977,6 +1024,7 @@ done:
         while (globaltimer() - t0 < 20000000ull) {
         }
     }
+    if (rank == 1 && warp < 4 && lane == 0) bulk_wait_all();  // each epilogue warp's stores have landed
     tc_fence_before();
     __syncthreads();
     cluster_sync();
@@ -1860,8 +1908,11 @@ int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const 
     CUtensorMap q_map;  // q as [T * N1 rows][D_qk], boxes of 64 dims x 64 head rows
     rc = make_map(&q_map, q, (int64_t)a.num_tokens * a.num_heads, a.head_dim, bf16, 64);
     if (rc) return rc;
+    CUtensorMap out_map;  // out as [T * N1 rows][D_v], boxes of 64 columns x 32 head rows (one warp's)
+    rc = make_map(&out_map, out, (int64_t)a.num_tokens * a.num_heads, a.v_head_dim, bf16, 32);
+    if (rc) return rc;
     // four instantiations of each kernel: element type x split
-    using KernelFn = void (*)(const TcArgs, const CUtensorMap, const CUtensorMap, const CUtensorMap);
+    using KernelFn = void (*)(const TcArgs, const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap);
     static const KernelFn kernels[4] = {fwd_tc_kernel<true, false>, fwd_tc_kernel<true, true>,
                                         fwd_tc_kernel<false, false>, fwd_tc_kernel<false, true>};
     using Kernel2Fn = void (*)(const TcArgs, const CUtensorMap, const CUtensorMap);
@@ -1901,7 +1952,7 @@ int launch_fwd_tc(const SasFwdArgs &a, const sas::FwdLayout &L, char *ws, const 
     cfg.attrs = attr;
     cfg.numAttrs = 2;
     cudaError_t e = pair ? cudaLaunchKernelEx(&cfg, kernels2[di], p, ori_map, cmp_map)
-                         : cudaLaunchKernelEx(&cfg, kernels[di], p, ori_map, cmp_map, q_map);
+                         : cudaLaunchKernelEx(&cfg, kernels[di], p, ori_map, cmp_map, q_map, out_map);
     if (check_cuda(e)) return SAS_ERR_CUDA;
     if (p.P > 1) {
         cudaLaunchConfig_t cc = {};
