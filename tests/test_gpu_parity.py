@@ -460,3 +460,27 @@ def test_head_counts_off_the_q_box(api, cuda_device, kernel, heads, q_lens):
         cmp_sparse_indices=wl_c.cmp_sparse_indices, cmp_ratio=wl_c.cmp_ratio, v_head_dim=wl_c.v_head_dim,
         tokens=sample)
     assert_close_to_golden(out[sample], lse[sample], ref_out[sample], ref_lse[sample], f"{kernel} h{heads}")
+
+
+@pytest.mark.parametrize("kernel", ["tc", "tc2"])
+@pytest.mark.parametrize("heads", [32, 64, 96])
+def test_whole_token_epilogue_head_counts(api, cuda_device, kernel, heads):
+    """Whole tokens (40 of them: no automatic split) with head counts below 128 that are multiples of
+    32: the tensor-core kernel's epilogue writes each warp's 32 head rows with its own TMA store and
+    warps past N1 write nothing; every sampled token must meet the golden bars."""
+    if not tc_available():
+        pytest.skip("tensor-core path not built")
+    from dsv4_planb_b200 import workloads as W
+
+    wl = W.make_workload(name=f"epi{heads}", q_lens=[1] * 40, kv_lens=[1500 + 91 * i for i in range(40)],
+                         num_heads=heads, topk=256, seed=51)
+    out, lse = run(api, wl, kernel, cuda_device)
+    sample = [0, 17, 39]
+    ref_out, ref_lse, _ = O.sparse_attn_sharedkv_oracle(
+        wl.q, ori_kv=wl.ori_kv, ori_block_table=wl.ori_block_table, seqused_kv=wl.seqused_kv,
+        q_prefix=wl.cu_seqlens_q[:-1], act_q=wl.cu_seqlens_q[1:] - wl.cu_seqlens_q[:-1], sinks=wl.sinks,
+        softmax_scale=wl.softmax_scale, cmp_kv=wl.cmp_kv, cmp_block_table=wl.cmp_block_table,
+        cmp_sparse_indices=wl.cmp_sparse_indices, cmp_ratio=wl.cmp_ratio, v_head_dim=wl.v_head_dim,
+        tokens=sample)
+    assert_close_to_golden(out[sample], lse[sample], ref_out[sample], ref_lse[sample], f"{kernel} h{heads}")
+    assert np.isfinite(out).all()
